@@ -1,0 +1,374 @@
+"""Benchmark of the B200 decode-attention hot path (BASELINE.json metric).
+
+Default workload (N=1): BASELINE config 2 — paged single-query decoder self-attention,
+fp16, B=64 sequences, 12 heads, head_dim 64, block_size 16, context ~ U[1,448], block
+tables from a seeded permutation of a 4096-block pool, q/K/V ~ N(0,1)*0.5, scale 1/8.
+A step is one launch of the paged attention kernel over one batch.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  (N > 1: launched by torch.distributed.run, one rank per GPU; each rank is an
+   independent replica on its own inputs — weak scaling, no data-path collective)
+
+Timing:
+  value  K steps replayed from one CUDA graph, each step reading a different one of 8
+         resident input sets (8 x ~44 MB touched > 126 MB L2, so reads come from HBM);
+         CUDA events on the replay stream; barrier + synchronize on both sides; the
+         max time over ranks; GB/s of algorithmic bytes (valid K/V rows + q + out +
+         tables + lengths) summed over ranks.
+  e2e    the same metric through the public API (speech_serving.ops) with pinned HOST
+         buffers: every step copies q/tables/lengths host->device, runs the op and copies
+         the output device->host, timed with CUDA events around the whole loop.
+  roofline  bytes per launch / average launch duration (graph replay time / K) against
+         the measured HBM copy bandwidth (MEASURED_PEAKS.json hbm_gbs).
+  cpu_baseline  the C port of the reference math (oracle/oracle.c, all host threads) on
+         a bounded sample of the same workload, rank 0 at N=1 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path[:0] = [str(REPO), str(REPO / "inference-speech-model_b200")]
+
+METRIC = "paged decode-attn HBM GB/s (% of 8 TB/s); decoder tokens/s at 1/2/4/8 GPU"
+FALLBACK_HBM_GBS = 6650.0
+N_SETS = 8
+
+CFG2 = dict(B=64, H=12, D=64, bs=16, num_blocks=4096, max_ctx=448, scale=0.125)
+
+
+def _peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def make_inputs(seed: int, device: str = "cpu"):
+    """Seeded config-2 batch.  Lengths and block tables come from a CPU generator (the
+    same on every host); the pool and query values are drawn on `device`."""
+    import torch
+
+    c = CFG2
+    g = torch.Generator().manual_seed(seed)
+    ctx = torch.randint(1, c["max_ctx"] + 1, (c["B"],), generator=g, dtype=torch.int32)
+    maxb = c["max_ctx"] // c["bs"]
+    perm = torch.randperm(c["num_blocks"], generator=g).to(torch.int32)
+    tables = perm[: c["B"] * maxb].view(c["B"], maxb).contiguous()
+    gd = torch.Generator(device=device).manual_seed(seed)
+    shape = (c["num_blocks"], c["bs"], c["H"], c["D"])
+    q = (torch.randn(c["B"], c["H"], c["D"], generator=gd, device=device) * 0.5).half()
+    kp = (torch.randn(shape, generator=gd, device=device) * 0.5).half()
+    vp = (torch.randn(shape, generator=gd, device=device) * 0.5).half()
+    return dict(q=q, k_pool=kp, v_pool=vp, tables=tables.to(device), ctx=ctx.to(device))
+
+
+def algorithmic_bytes(ctx) -> int:
+    """Bytes one launch must move: every valid K and V row of every head, plus q, out,
+    block-table entries actually read and the lengths."""
+    c = CFG2
+    ctx = [int(x) for x in ctx]
+    kv = sum(ctx) * c["H"] * c["D"] * 2 * 2
+    qo = 2 * c["B"] * c["H"] * c["D"] * 2
+    tab = sum(-(-x // c["bs"]) for x in ctx) * 4 + c["B"] * 4
+    return kv + qo + tab
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons every 200 ms in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu = gpu_id
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i, v in enumerate(r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def cpu_baseline(seconds: float = 10.0, threads: int | None = None):
+    """Times the C port of the reference math on the host cores over config-2 batches."""
+    from oracle import c_oracle
+
+    threads = threads or os.cpu_count()
+    d = make_inputs(1000)  # on the host
+    args = [d["q"].numpy(), d["k_pool"].numpy(), d["v_pool"].numpy(), d["tables"].numpy(), d["ctx"].numpy()]
+    nbytes = algorithmic_bytes(d["ctx"])
+    c_oracle.paged_decode_attention(*args, CFG2["scale"], threads=threads)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        c_oracle.paged_decode_attention(*args, CFG2["scale"], threads=threads)
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(nbytes * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} config-2 batches (B=64, fp16 pools) in {dt:.1f} s, oracle/oracle.c OpenMP"}
+
+
+def dist_setup(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def run_reference(args):
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import c_oracle
+
+    threads = os.cpu_count()
+    d = make_inputs(1000)
+    a = [d["q"].numpy(), d["k_pool"].numpy(), d["v_pool"].numpy(), d["tables"].numpy(), d["ctx"].numpy()]
+    nbytes = algorithmic_bytes(d["ctx"])
+    for _ in range(args.warmup):
+        c_oracle.paged_decode_attention(*a, CFG2["scale"], threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        c_oracle.paged_decode_attention(*a, CFG2["scale"], threads=threads)
+    dt = time.perf_counter() - t0
+    v = nbytes * args.steps / dt / 1e9
+    line = {"metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 in, f32 arithmetic", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "config 2: paged decode self-attention B=64 H=12 D=64 bs=16 ctx~U[1,448]",
+                       "global_batch": CFG2["B"], "seq_len": CFG2["max_ctx"], "parallelism": "host threads"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} config-2 batches, oracle/oracle.c OpenMP (the reference is "
+                                       "PyTorch with no native CPU library; this is its arithmetic ported to C)"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from speech_serving import ops
+
+    c = CFG2
+    sets = [make_inputs(1000 + 97 * rank + i, device=dev) for i in range(N_SETS)]
+    outs = [torch.empty(c["B"], c["H"], c["D"], dtype=torch.float16, device=dev) for _ in range(N_SETS)]
+    ws = ops.paged_attn_workspace(c["B"], c["H"], c["D"], dev)
+    bytes_per = [algorithmic_bytes(s["ctx"].cpu()) for s in sets]
+
+    def launch(i):
+        s = sets[i % N_SETS]
+        ops.paged_decode_attention(s["q"], s["k_pool"], s["v_pool"], s["tables"], s["ctx"], scale=c["scale"],
+                                   out=outs[i % N_SETS], workspace=ws)
+
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            launch(i)
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(args.steps):
+            launch(i)
+    for _ in range(max(args.warmup, 3) // args.steps + 1):
+        graph.replay()  # warm the graph itself
+    torch.cuda.synchronize()
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pr = torch.cuda.get_device_properties(dev)
+    sampler = ClockSampler(f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0")
+
+    def sustain(seconds):
+        # untimed replays of the same graph so the clock samples see this load
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end:
+            graph.replay()
+            torch.cuda.synchronize()
+
+    with sampler:
+        sustain(0.6)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        sustain(0.6)
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    bytes_rank = sum(bytes_per[i % N_SETS] for i in range(args.steps))
+    value = bytes_rank * world / (ms_max / 1e3) / 1e9
+    launch_ms = ms / args.steps
+    achieved = (bytes_rank / args.steps) / (launch_ms / 1e3) / 1e9
+
+    # ---- e2e through the public API with pinned host buffers ----------------------
+    hq = [s["q"].cpu().pin_memory() for s in sets]
+    ht = [s["tables"].cpu().pin_memory() for s in sets]
+    hc = [s["ctx"].cpu().pin_memory() for s in sets]
+    hout = [torch.empty(c["B"], c["H"], c["D"], dtype=torch.float16).pin_memory() for _ in range(N_SETS)]
+    dq = torch.empty_like(sets[0]["q"])
+    dt_ = torch.empty_like(sets[0]["tables"])
+    dc = torch.empty_like(sets[0]["ctx"])
+    dout = torch.empty_like(outs[0])
+
+    def e2e_step(i):
+        j = i % N_SETS
+        dq.copy_(hq[j], non_blocking=True)
+        dt_.copy_(ht[j], non_blocking=True)
+        dc.copy_(hc[j], non_blocking=True)
+        ops.paged_decode_attention(dq, sets[j]["k_pool"], sets[j]["v_pool"], dt_, dc, scale=c["scale"], out=dout,
+                                   workspace=ws)
+        hout[j].copy_(dout, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            e2e_step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(args.steps):
+            e2e_step(i)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_value = bytes_rank * world / (float(et.item()) / 1e3) / 1e9
+    h2d = dq.numel() * 2 + dt_.numel() * 4 + dc.numel() * 4
+    d2h = dout.numel() * 2
+
+    # correctness guard on the timed data: one set against the oracle's C port
+    ok_err = None
+    if rank == 0:
+        from oracle import c_oracle
+        import numpy as np
+
+        s0 = sets[0]
+        ref = c_oracle.paged_decode_attention(s0["q"].cpu().numpy(), s0["k_pool"].cpu().numpy(),
+                                              s0["v_pool"].cpu().numpy(), s0["tables"].cpu().numpy(),
+                                              s0["ctx"].cpu().numpy(), c["scale"])
+        ops.paged_decode_attention(s0["q"], s0["k_pool"], s0["v_pool"], s0["tables"], s0["ctx"], scale=c["scale"],
+                                   out=outs[0], workspace=ws)
+        ok_err = float(np.abs(outs[0].float().cpu().numpy() - ref).max())
+        if ok_err > 2e-3:
+            raise RuntimeError(f"benchmark output differs from the oracle by {ok_err}")
+        if ops.read_error_word(ws) != 0:
+            raise RuntimeError("kernel reported a device error during the benchmark")
+
+    if world > 1:
+        dist.barrier()
+        del graph
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, peak_kind = _peaks()
+    traffic = None
+    tf = REPO / "profiles" / "ncu_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("paged_decode_attn_config2_bytes_per_launch")
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 in, f32 arithmetic", "data": "synthetic",
+        "config": {"workload": "config 2: paged decode self-attention B=64 H=12 D=64 bs=16 ctx~U[1,448] "
+                               "4096-block pool per input set",
+                   "global_batch": CFG2["B"] * world, "seq_len": CFG2["max_ctx"], "parallelism": f"replicas x{world}",
+                   "l2": f"inputs rotate over {N_SETS} resident sets (~{N_SETS * bytes_per[0] / 1e6:.0f} MB touched "
+                         "per rotation > 126 MB L2)",
+                   "timing": "CUDA graph of K launches, CUDA events, max over ranks"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} hbm_gbs (copy bandwidth)",
+                     "bytes_per_launch": int(bytes_rank / args.steps), "launch_us": round(launch_ms * 1e3, 3)},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "speech_serving.ops.paged_decode_attention (ctypes -> C ABI), pinned host buffers"},
+        "gpu_launches": args.steps,
+        "clocks": sampler.summary(),
+        "max_abs_err_vs_oracle": ok_err,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,63 @@
+// spd_params.cuh — kernel parameter blocks shared by the kernels and the ABI layer.
+// Passed to kernels by value (they live in the constant parameter bank).
+#pragma once
+
+#include "spd_common.cuh"
+
+namespace spd {
+
+struct PagedParams {
+  const void* q;
+  void* k_pool;
+  void* v_pool;
+  const int* block_tables;
+  const int* context_lens;
+  void* out;
+  const void* k_new;
+  const void* v_new;
+  int B, H, max_blocks, num_blocks;
+  float scale_log2;  // scale * log2(e)
+  int* err;          // workspace error word
+  int* counters;     // [B] arrival counters (left at zero)
+  float* partials;   // [(B + grid) * H * (D + 2)]
+  int stages;
+};
+
+struct CrossParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int* valid_lens;
+  void* out;
+  int B, H, T_max;
+  long long kv_batch_stride, kv_head_stride;  // elements
+  float scale_log2;
+  int* err;
+  int* counters;    // [B*H]
+  float* partials;  // [(B*H + grid) * (D + 2)]
+  int stages;
+};
+
+struct AppendParams {
+  const unsigned char* k_src;
+  const unsigned char* v_src;
+  long long sb, sh, st;  // source strides in bytes
+  unsigned char* k_pool;
+  unsigned char* v_pool;
+  const int* block_tables;
+  const int* positions;
+  int B, T, H, row_bytes, block_size, max_blocks, num_blocks;
+  int* err;
+};
+
+struct GatherParams {
+  const unsigned char* pool;
+  const int* block_tables;
+  const int* seq_lens;
+  unsigned char* out;
+  int B, H, row_bytes, block_size, max_blocks, num_blocks, T_out, zero_pad;
+  long long out_batch_stride;  // bytes
+  int* err;
+};
+
+}  // namespace spd
