@@ -79,7 +79,7 @@ GEOMS = [  # (H, D, block_size)
 def test_paged_attention_matches_oracle(H, D, bs, dtype):
     if H * D * bs * (4 if dtype == torch.float32 else 2) * 2 > 220 * 1024:
         pytest.skip("one pool block of K and V exceeds shared memory (reported as SPD_ERR_UNSUPPORTED)")
-    rng = np.random.default_rng(abs(hash((H, D, bs, str(dtype)))) % 2**32)
+    rng = np.random.default_rng(H * 100_000 + D * 100 + bs + 7 * [torch.float16, torch.bfloat16, torch.float32].index(dtype))
     B = 9
     ctx = np.array([1, bs, bs + 1, 0, 3 * bs - 1, 200, 448, 77, 2], np.int32)
     nb = int(sum(-(-c // bs) for c in ctx)) + 8
