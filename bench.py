@@ -311,6 +311,7 @@ def run_ours(args):
         ref = c_oracle.paged_decode_attention(s0["q"].cpu().numpy(), s0["k_pool"].cpu().numpy(),
                                               s0["v_pool"].cpu().numpy(), s0["tables"].cpu().numpy(),
                                               s0["ctx"].cpu().numpy(), c["scale"])
+        outs[0].fill_(float("nan"))  # an unwritten output cannot pass on stale values
         ops.paged_decode_attention(s0["q"], s0["k_pool"], s0["v_pool"], s0["tables"], s0["ctx"], scale=c["scale"],
                                    out=outs[0], workspace=ws)
         ok_err = float(np.abs(outs[0].float().cpu().numpy() - ref).max())

@@ -71,8 +71,9 @@ int spd_get_last_error(char* buf, size_t size);
 /* Number of bytes of workspace the attention kernels need.  The workspace holds a
  * 256-byte header (device error word at offset 0), per-sequence arrival counters and
  * fp32 split-KV partial results.  It must be zero-filled once before first use; the
- * kernels leave every counter back at zero, so it can be reused by later calls on the
- * same stream (calls that overlap on the GPU must use separate workspaces).
+ * kernels leave every counter back at zero, so it can be reused by later calls with the
+ * same (B, H, D) on the same stream.  A workspace used with another geometry must be
+ * zero-filled again first; calls that overlap on the GPU must use separate workspaces.
  * `device` < 0 means the current device. */
 size_t spd_paged_decode_attn_workspace_size(int B, int H, int D, int device);
 size_t spd_cross_attn_workspace_size(int B, int H, int D, int device);
@@ -137,18 +138,21 @@ int spd_block_gather(const void* pool, const int32_t* block_tables, const int32_
                      int dtype, int32_t* error_word, void* stream);
 
 /* (4) Cross-KV projection at encoder handoff: one tcgen05 GEMM for all decoder layers.
- *   enc_out [B][T][d_model]                         (row-major, dtype F16 or BF16)
- *   w_kv    [L*2*H*D][d_model]  rows ordered (layer, k|v, head, dim) — the k_proj and
- *                               v_proj weights of every decoder layer stacked
- *   b_kv    [L*2*H*D] or NULL   bias (zeros where a projection has none)
- *   out     element (b,l,kv,h,t,d) at out + slot(b)*out_slot_stride
- *                               + ((l*2 + kv)*H + h)*out_head_stride*... see below
- *           written as out + s*out_slot_stride + ((l*2+kv)*H + h)*T_out*D + t*D + d with
- *           s = slot_ids ? slot_ids[b] : b  (graph-slot layout [S][L][2][H][T_out][D]).
- * Requires d_model % 64 == 0, H*D % 64 == 0, T <= T_out. */
+ *   enc_out [B][T][d_model]          row-major encoder output (dtype F16 or BF16)
+ *   w_kv    [L*2*H*D][d_model]       the k_proj and v_proj weights of every decoder layer
+ *                                    stacked in (layer, k|v, head, dim) row order
+ *   b_kv    [L*2*H*D] or NULL        bias in the same order (zeros where a projection has
+ *                                    none: Whisper's k_proj has no bias, v_proj has one)
+ *   out     element (b, l, kv, h, t, d) is written at
+ *             out + s*out_slot_stride + (((l*2 + kv)*H + h)*T_out + t)*D + d,
+ *           s = slot_ids ? slot_ids[b] : b   — the graph-slot layout [S][L][2][H][T_out][D]
+ *   error_word: optional int32 device word receiving SPD_DEVERR_TIMEOUT.
+ * fp32 accumulation; output rounded to dtype.  Requires d_model % 64 == 0, D % 8 == 0,
+ * T <= T_out, 16-byte aligned pointers and slot stride. */
 int spd_cross_kv_project(const void* enc_out, const void* w_kv, const void* b_kv, void* out,
                          const int32_t* slot_ids, int B, int T, int d_model, int L, int H,
-                         int D, int T_out, int64_t out_slot_stride, int dtype, void* stream);
+                         int D, int T_out, int64_t out_slot_stride, int dtype,
+                         int32_t* error_word, void* stream);
 
 #ifdef __cplusplus
 }

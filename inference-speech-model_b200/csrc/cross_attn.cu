@@ -89,13 +89,17 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
   __syncthreads();
 
   const long long W = prefix[B];
-  const int c = blockIdx.x, G = gridDim.x;
-  for (int b = c; b < B; b += G) {
+  // Effective grid: never more CTAs than units, so every participating CTA owns at
+  // least one unit and the CTAs sharing a segment are consecutive (which the
+  // arrival count nparts = c_last - c_first + 1 relies on).
+  const int c = blockIdx.x;
+  const int G = (int)((long long)gridDim.x < W ? (long long)gridDim.x : W);
+  for (int b = c; b < B; b += gridDim.x) {
     if (val_s[b] == 0) {
       for (int i = tid; i < H * D; i += blockDim.x) out[(size_t)b * H * D + i] = Elem<T>::from_f(0.f);
     }
   }
-  if (W == 0) return;
+  if (W == 0 || c >= G) return;
   const long long start = range_start(c, G, W), end = range_start(c + 1, G, W);
   if (start >= end) return;
 

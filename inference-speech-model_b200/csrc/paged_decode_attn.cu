@@ -98,15 +98,19 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
   __syncthreads();
 
   const long long W = prefix[B];
-  const int c = blockIdx.x, G = gridDim.x;
+  // Effective grid: never more CTAs than units, so every participating CTA owns at
+  // least one unit and the CTAs sharing a segment are consecutive (which the
+  // arrival count nparts = c_last - c_first + 1 relies on).
+  const int c = blockIdx.x;
+  const int G = (int)((long long)gridDim.x < W ? (long long)gridDim.x : W);
 
   // ---- 2. sequences with nothing to attend to get zeros (CTA b % G) ---------------
-  for (int b = c; b < B; b += G) {
+  for (int b = c; b < B; b += gridDim.x) {
     if (prefix[b + 1] == prefix[b]) {
       for (int i = tid; i < HD; i += nthreads) out[(size_t)b * HD + i] = Elem<T>::from_f(0.f);
     }
   }
-  if (W == 0) return;
+  if (W == 0 || c >= G) return;
   const long long start = range_start(c, G, W), end = range_start(c + 1, G, W);
   if (start >= end) return;
 

@@ -18,7 +18,7 @@ int kv_append_launch(const AppendParams& p, int sms, cudaStream_t st);
 int block_gather_launch(const GatherParams& p, int sms, cudaStream_t st);
 int cross_kv_project_launch(const void* enc_out, const void* w_kv, const void* b_kv, void* out,
                             const int32_t* slot_ids, int B, int T, int d_model, int L, int H, int D,
-                            int T_out, int64_t out_slot_stride, int dtype, int sms, cudaStream_t st);
+                            int T_out, int64_t out_slot_stride, int dtype, int* err, int sms, cudaStream_t st);
 }  // namespace spd
 
 namespace {
@@ -247,14 +247,14 @@ int spd_block_gather(const void* pool, const int32_t* block_tables, const int32_
 
 int spd_cross_kv_project(const void* enc_out, const void* w_kv, const void* b_kv, void* out,
                          const int32_t* slot_ids, int B, int T, int d_model, int L, int H, int D, int T_out,
-                         int64_t out_slot_stride, int dtype, void* stream) {
+                         int64_t out_slot_stride, int dtype, int32_t* error_word, void* stream) {
   if (dtype != SPD_F16 && dtype != SPD_BF16)
     return fail(SPD_ERR_UNSUPPORTED, "spd_cross_kv_project: dtype %d not supported (F16/BF16 only)", dtype);
   if (!enc_out || !w_kv || !out) return fail(SPD_ERR_INVALID_ARG, "spd_cross_kv_project: null pointer");
   if (B <= 0 || T <= 0 || d_model <= 0 || L <= 0 || H <= 0 || D <= 0 || T_out < T)
     return fail(SPD_ERR_INVALID_ARG, "spd_cross_kv_project: bad sizes");
-  if (d_model % 64 || (H * D) % 64 || D % 8)
-    return fail(SPD_ERR_UNSUPPORTED, "spd_cross_kv_project: need d_model %% 64 == 0, H*D %% 64 == 0, D %% 8 == 0");
+  if (d_model % 64 || D % 8)
+    return fail(SPD_ERR_UNSUPPORTED, "spd_cross_kv_project: need d_model %% 64 == 0 and D %% 8 == 0");
   if (!aligned16(enc_out) || !aligned16(w_kv) || !aligned16(out) || (b_kv && !aligned16(b_kv)) ||
       (out_slot_stride * 2) % 16)
     return fail(SPD_ERR_INVALID_ARG, "spd_cross_kv_project: pointers and strides must be 16-byte aligned");
@@ -263,7 +263,8 @@ int spd_cross_kv_project(const void* enc_out, const void* w_kv, const void* b_kv
   const int sms = sm_count(-1);
   if (sms <= 0) return fail(SPD_ERR_CUDA, "spd_cross_kv_project: no CUDA device");
   const int rc = spd::cross_kv_project_launch(enc_out, w_kv, b_kv, out, slot_ids, B, T, d_model, L, H, D, T_out,
-                                              out_slot_stride, dtype, sms, static_cast<cudaStream_t>(stream));
+                                              out_slot_stride, dtype, error_word, sms,
+                                              static_cast<cudaStream_t>(stream));
   if (rc == SPD_ERR_UNSUPPORTED) return fail(rc, "spd_cross_kv_project: shape not supported");
   if (rc != SPD_OK) return fail(rc, "spd_cross_kv_project: launch failed: %s", cudaGetErrorString(cudaGetLastError()));
   return ok();

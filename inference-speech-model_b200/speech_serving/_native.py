@@ -43,7 +43,7 @@ _SIGNATURES = {
     "spd_kv_append": (_i, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i,
                            _vp, _vp]),
     "spd_block_gather": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _i, _i, _vp, _vp]),
-    "spd_cross_kv_project": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _i, _vp]),
+    "spd_cross_kv_project": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _i, _vp, _vp]),
 }
 
 _lib = None

@@ -81,12 +81,13 @@ def cross_attn_workspace(B: int, H: int, D: int, device: torch.device) -> torch.
 
 
 def _cached_workspace(kind: str, B: int, H: int, D: int, device: torch.device) -> torch.Tensor:
-    key = (kind, device, torch.cuda.current_stream(device).cuda_stream)
+    """One zero-initialised workspace per (op, geometry, device, stream).  The counter and
+    partial regions are laid out by geometry, so a workspace is never shared between
+    geometries (stale partials would otherwise land in another call's counters)."""
+    key = (kind, B, H, D, device, torch.cuda.current_stream(device).cuda_stream)
     ws = _WORKSPACES.get(key)
-    need = (N.load().spd_paged_decode_attn_workspace_size if kind == "paged" else
-            N.load().spd_cross_attn_workspace_size)(B, H, D, device.index)
-    if ws is None or ws.numel() < need:
-        ws = torch.zeros(need, dtype=torch.uint8, device=device)
+    if ws is None:
+        ws = (paged_attn_workspace if kind == "paged" else cross_attn_workspace)(B, H, D, device)
         _WORKSPACES[key] = ws
     return ws
 
