@@ -6,7 +6,7 @@
 namespace spd {
 
 int cross_kv_project_launch(const void*, const void*, const void*, void*, const int32_t*, int, int, int, int,
-                            int, int, int, int64_t, int, int, cudaStream_t) {
+                            int, int, int, int64_t, int, int*, int, cudaStream_t) {
   return SPD_ERR_UNSUPPORTED;
 }
 
