@@ -1,13 +1,279 @@
-// cross_kv_project.cu — op (4): cross-KV projection GEMM at encoder handoff
-// (speech_serving/models.py:554-561).  The tcgen05 implementation is added in this
-// file; until it is present the entry point reports SPD_ERR_UNSUPPORTED.
+// cross_kv_project.cu — op (4): the cross-KV projection at encoder handoff as one
+// tcgen05 GEMM over every decoder layer.
+//
+// Reference: speech_serving/models.py:554-561 runs, per decoder layer,
+//   k = encoder_attn.k_proj(enc_out)   (no bias)      -> view [B,T,H,D] -> transpose(1,2)
+//   v = encoder_attn.v_proj(enc_out)   (+ bias)       -> view [B,T,H,D] -> transpose(1,2)
+// i.e. 2*L GEMMs [B*T, d] x [d, H*D] plus 2*L transpose copies.  Here the k_proj/v_proj
+// weights of all layers are stacked into W [L*2*H*D, d] and ONE GEMM
+//   C[m, n] = sum_k A[m, k] * W[n, k] + bias[n],   A = enc_out viewed [B*T, d]
+// is computed, with the epilogue writing C straight into the graph-slot layout
+// [S][L][2][H][T_out][D] (no transpose copies).
+//
+// sm_100a design: one 128x256 output tile per CTA (4 warps).  Warp 0 lane 0 issues
+// 2-D TMA loads (128-byte swizzle, no multicast) of the A and W tiles for each 64-wide
+// K slice into a 4-stage shared-memory ring (full/empty mbarriers); warp 1 lane 0
+// issues tcgen05.mma (kind::f16, M=128, N=256, K=16, fp32 accumulator in 256 TMEM
+// columns) and frees each stage with tcgen05.commit; after the last K slice a commit
+// signals the epilogue, where each of the 128 threads owns one accumulator row (TMEM
+// lane), reads it with tcgen05.ld, adds the bias in fp32, rounds and stores 16-byte
+// runs of one head's row.  All waits are bounded (SPD_DEVERR_TIMEOUT on expiry).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "spd_params.cuh"
 
 namespace spd {
 
-int cross_kv_project_launch(const void*, const void*, const void*, void*, const int32_t*, int, int, int, int,
-                            int, int, int, int64_t, int, int*, int, cudaStream_t) {
-  return SPD_ERR_UNSUPPORTED;
+namespace proj {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;  // 64 x 2 bytes = one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int TMEM_COLS = 256;
+constexpr size_t SMEM_BYTES = 1024 /*alignment slack*/ + (size_t)STAGES * (A_BYTES + B_BYTES) + 256;
+
+struct Params {
+  const void* bias;      // [N] or null
+  void* out;
+  const int* slot_ids;   // [B] or null
+  int M, N, K, T, H, D, T_out;
+  long long out_slot_stride;  // elements
+  int* err;
+};
+
+// ---- PTX wrappers (tcgen05 / TMA) -----------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// 16 consecutive fp32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of 128 B in
+// 8-row (1024 B) swizzle atoms stacked along M/N (stride byte offset 1024).
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
+  const uint64_t addr = smem_addr(tile);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;          // start address
+  d |= (uint64_t)1 << 16;                // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;      // stride byte offset
+  d |= (uint64_t)1 << 46;                // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulate, A/B both fp16 or both bf16,
+// both K-major, M = 128, N = BN.
+__host__ __device__ constexpr uint32_t instr_desc(bool bf16) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128, 1)
+    cross_kv_project_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                            const Params p) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t base_addr = smem_addr(smem_raw);
+  unsigned char* smem = smem_raw + ((1024 - (base_addr & 1023)) & 1023);  // 1024-aligned for SW128
+  unsigned char* a_tiles = smem;
+  unsigned char* b_tiles = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(b_tiles + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int nk = p.K / BK;
+  constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ------------------------------------------------------------
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % STAGES;
+      if (kb >= STAGES && !mbar_wait_bounded(&empty[s], ((kb / STAGES) & 1) ^ 1, p.err)) break;
+      mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+      tma_load_2d(a_tiles + s * A_BYTES, &tm_a, kb * BK, m0, &full[s]);
+      tma_load_2d(b_tiles + s * B_BYTES, &tm_b, kb * BK, n0, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----------------------------------------------------------------
+    constexpr uint32_t idesc = instr_desc(kBf16);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % STAGES;
+      if (!mbar_wait_bounded(&full[s], (kb / STAGES) & 1, p.err)) break;
+      tc_fence_after();
+      const uint64_t da = smem_desc_sw128(a_tiles + s * A_BYTES);
+      const uint64_t db = smem_desc_sw128(b_tiles + s * B_BYTES);
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k) {
+        // each K=16 step advances 32 bytes inside the 128-byte swizzle row
+        umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+      }
+      umma_commit(&empty[s]);
+    }
+    umma_commit(acc_full);
+  }
+  __syncwarp();
+
+  // ---- epilogue: thread = accumulator row (TMEM lane 32*warp + lane) --------------------
+  const bool ready = mbar_wait_bounded(acc_full, 0, p.err);
+  __syncwarp();
+  tc_fence_after();
+  const int m = m0 + warp * 32 + lane;
+  const bool row_ok = ready && m < p.M;
+  const int b = row_ok ? m / p.T : 0;
+  const int t = row_ok ? m % p.T : 0;
+  const long long slot = row_ok ? (p.slot_ids ? p.slot_ids[b] : b) : 0;
+  T* out = reinterpret_cast<T*>(p.out) + slot * p.out_slot_stride + (long long)t * p.D;
+  const T* bias = reinterpret_cast<const T*>(p.bias);
+  const int HD = p.H * p.D;
+  const long long plane = (long long)p.T_out * p.D;  // one (layer, k|v, head) plane
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 16) {
+    float v[16];
+    tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);  // all lanes, aligned
+    if (!row_ok) continue;
+#pragma unroll
+    for (int g = 0; g < 16; g += 8) {
+      const int n = n0 + c0 + g;
+      if (n >= p.N) break;
+      const int lkv = n / HD, rem = n % HD;
+      const int h = rem / p.D, d = rem % p.D;
+      alignas(16) T o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float x = v[g + i];
+        if (bias) x += Elem<T>::to_f(bias[n + i]);
+        o[i] = Elem<T>::from_f(x);
+      }
+      *reinterpret_cast<uint4*>(out + ((long long)lkv * p.H + h) * plane + d) = *reinterpret_cast<uint4*>(o);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ---- host side ------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// Row-major [rows][inner] 16-bit matrix, box [box_rows][64] with 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* base, int inner, int rows, int box_rows, bool bf16) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace proj
+
+int cross_kv_project_launch(const void* enc_out, const void* w_kv, const void* b_kv, void* out,
+                            const int32_t* slot_ids, int B, int T, int d_model, int L, int H, int D, int T_out,
+                            int64_t out_slot_stride, int dtype, int* err, int sms, cudaStream_t st) {
+  (void)sms;
+  using namespace proj;
+  const bool bf16 = dtype == SPD_BF16;
+  const long long M = (long long)B * T, N = (long long)L * 2 * H * D;
+  if (M > (1ll << 31) - 1 || N > (1ll << 31) - 1 || (N % 8)) return SPD_ERR_UNSUPPORTED;
+  CUtensorMap ta, tb;
+  if (!make_map(&ta, enc_out, d_model, (int)M, BM, bf16) || !make_map(&tb, w_kv, d_model, (int)N, BN, bf16))
+    return SPD_ERR_CUDA;
+  Params p{};
+  p.bias = b_kv; p.out = out; p.slot_ids = slot_ids;
+  p.M = (int)M; p.N = (int)N; p.K = d_model; p.T = T; p.H = H; p.D = D; p.T_out = T_out;
+  p.out_slot_stride = out_slot_stride; p.err = err;
+  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
+  if (bf16) {
+    auto k = cross_kv_project_kernel<__nv_bfloat16>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess)
+      return SPD_ERR_CUDA;
+    k<<<grid, 128, SMEM_BYTES, st>>>(ta, tb, p);
+  } else {
+    auto k = cross_kv_project_kernel<__half>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess)
+      return SPD_ERR_CUDA;
+    k<<<grid, 128, SMEM_BYTES, st>>>(ta, tb, p);
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? SPD_OK : SPD_ERR_CUDA;
 }
 
 }  // namespace spd

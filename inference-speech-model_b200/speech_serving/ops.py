@@ -270,3 +270,59 @@ def block_gather(
         _ptr(error_word), _stream_handle())
     N.check(rc, "spd_block_gather")
     return out
+
+
+# ----------------------------------------------------------------------------- op (4)
+def stack_cross_kv_weights(layers) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Stacks every decoder layer's cross-attention k_proj / v_proj into the GEMM operand
+    of ``cross_kv_project``: W [L*2*H*D, d_model] in (layer, k|v, head, dim) row order and
+    the matching bias (zeros for k_proj, which has none; speech_serving/models.py:557-559,
+    transformers WhisperAttention k_proj bias=False, v_proj bias=True)."""
+    ws, bs = [], []
+    for layer in layers:
+        att = layer.encoder_attn
+        for proj in (att.k_proj, att.v_proj):
+            ws.append(proj.weight)
+            bs.append(proj.bias if proj.bias is not None else torch.zeros(proj.weight.shape[0], dtype=proj.weight.dtype,
+                                                                          device=proj.weight.device))
+    return torch.cat(ws, 0).contiguous(), torch.cat(bs, 0).contiguous()
+
+
+def cross_kv_project(
+    enc_out: torch.Tensor,
+    w_kv: torch.Tensor,
+    b_kv: Optional[torch.Tensor],
+    out: torch.Tensor,
+    slot_ids: Optional[torch.Tensor] = None,
+    error_word: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """One tcgen05 GEMM that projects the encoder output into every decoder layer's
+    cross-attention K and V, written into the graph-slot layout.
+
+    enc_out [B, T, d_model]; w_kv [L*2*H*D, d_model] (``stack_cross_kv_weights``);
+    b_kv [L*2*H*D] or None; out [S, L, 2, H, T_out, D] with T <= T_out (rows t >= T
+    untouched); slot_ids int32 [B] picks each request's slot (default: slot b)."""
+    _require_cuda("cross_kv_project", enc_out, w_kv, b_kv, out, slot_ids, error_word)
+    if enc_out.dim() != 3 or not enc_out.is_contiguous() or not w_kv.is_contiguous():
+        raise RuntimeError("cross_kv_project: enc_out [B, T, d_model] and w_kv must be contiguous")
+    B, T, d = enc_out.shape
+    if out.dim() != 6 or not out.is_contiguous():
+        raise RuntimeError("cross_kv_project: out must be a contiguous [S, L, 2, H, T_out, D] tensor")
+    S, L, two, H, T_out, D = out.shape
+    if two != 2 or w_kv.shape != (L * 2 * H * D, d) or T > T_out:
+        raise RuntimeError(f"cross_kv_project: w_kv {tuple(w_kv.shape)} / out {tuple(out.shape)} / T={T} mismatch")
+    if b_kv is not None and (b_kv.shape != (L * 2 * H * D,) or not b_kv.is_contiguous()):
+        raise RuntimeError("cross_kv_project: b_kv must be a contiguous [L*2*H*D] tensor")
+    for t in (w_kv, b_kv, out):
+        if t is not None and t.dtype != enc_out.dtype:
+            raise RuntimeError("cross_kv_project: all tensors must share enc_out's dtype")
+    if slot_ids is not None:
+        if slot_ids.dtype != torch.int32 or slot_ids.shape != (B,):
+            raise RuntimeError("cross_kv_project: slot_ids must be int32 [B]")
+    elif B > S:
+        raise RuntimeError("cross_kv_project: more requests than slots and no slot_ids")
+    rc = N.load().spd_cross_kv_project(
+        enc_out.data_ptr(), w_kv.data_ptr(), _ptr(b_kv), out.data_ptr(), _ptr(slot_ids), B, T, d, L, H, D, T_out,
+        out.stride(0), dtype_code(enc_out.dtype), _ptr(error_word), _stream_handle())
+    N.check(rc, "spd_cross_kv_project")
+    return out

@@ -1,0 +1,81 @@
+"""Runs one named kernel workload a few times with plain launches, for profilers.
+
+    python -m speech_serving.profile_cases paged_cfg2 --launches 3
+    python -m speech_serving.profile_cases cross_cfg3 --launches 3
+    python -m speech_serving.profile_cases proj_small --launches 3
+
+Cases: paged_cfg2 = paged self-attention B=64 H=12 D=64 bs=16
+ctx~U[1,448] fp16; cross_cfg3 = cross-attention B=128 H=20 D=64 T=1500 valid~U[300,1500]
+bf16; proj_small / proj_large = the handoff cross-KV projection of one 1500-position
+request for Whisper-small (d 768, 12 layers x 12 heads) / large-v3 (d 1280, 32 x 20), bf16.
+Each launch reads a different input set so that DRAM counters see cold data.
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+from . import ops
+
+
+def _paged(dev, sets):
+    g = torch.Generator().manual_seed(0)
+    B, H, D, bs, NB = 64, 12, 64, 16, 4096
+    out = []
+    for i in range(sets):
+        ctx = torch.randint(1, 449, (B,), generator=g, dtype=torch.int32)
+        tables = torch.randperm(NB, generator=g)[: B * 28].view(B, 28).to(torch.int32)
+        q = torch.randn(B, H, D, device=dev).half()
+        kp = torch.randn(NB, bs, H, D, device=dev).half()
+        vp = torch.randn(NB, bs, H, D, device=dev).half()
+        out.append((q, kp, vp, tables.to(dev), ctx.to(dev)))
+    ws = ops.paged_attn_workspace(B, H, D, dev)
+    return lambda i: ops.paged_decode_attention(*out[i % sets], scale=0.125, workspace=ws)
+
+
+def _cross(dev, sets):
+    g = torch.Generator().manual_seed(0)
+    B, H, T, D = 128, 20, 1500, 64
+    out = []
+    for i in range(sets):
+        valid = torch.randint(300, 1501, (B,), generator=g, dtype=torch.int32)
+        out.append((torch.randn(B, H, D, device=dev).bfloat16(), torch.randn(B, H, T, D, device=dev).bfloat16(),
+                    torch.randn(B, H, T, D, device=dev).bfloat16(), valid.to(dev)))
+    ws = ops.cross_attn_workspace(B, H, D, dev)
+    return lambda i: ops.cross_attention(*out[i % sets], scale=0.125, workspace=ws)
+
+
+def _proj(dev, sets, d, L, H):
+    D, T = 64, 1500
+    enc = [torch.randn(1, T, d, device=dev).bfloat16() for _ in range(sets)]
+    w = (torch.randn(L * 2 * H * D, d, device=dev) * 0.02).bfloat16()
+    b = torch.zeros(L * 2 * H * D, device=dev).bfloat16()
+    out = torch.empty((1, L, 2, H, T, D), device=dev, dtype=torch.bfloat16)
+    return lambda i: ops.cross_kv_project(enc[i % sets], w, b, out)
+
+
+CASES = {
+    "paged_cfg2": lambda dev, n: _paged(dev, n),
+    "cross_cfg3": lambda dev, n: _cross(dev, n),
+    "proj_small": lambda dev, n: _proj(dev, n, 768, 12, 12),
+    "proj_large": lambda dev, n: _proj(dev, n, 1280, 32, 20),
+}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=sorted(CASES))
+    ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--sets", type=int, default=2)
+    a = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    run = CASES[a.case](dev, a.sets)
+    for i in range(a.launches):
+        run(i)
+    torch.cuda.synchronize()
+    print(f"{a.case}: {a.launches} launches ok")
+
+
+if __name__ == "__main__":
+    main()
