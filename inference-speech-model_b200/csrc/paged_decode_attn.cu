@@ -11,55 +11,119 @@
 // B200 design (HBM-bound; no tensor cores):
 // * Work units are pool blocks.  A unit covers one block of ALL heads, which in the
 //   pool layout [num_blocks][block_size][H][D] is one contiguous run of
-//   block_size*H*D elements, so each unit is fetched with two 1-D bulk async copies
-//   (K and V; only the valid rows of a sequence's last block are copied).
+//   block_size*H*D elements, fetched with two 1-D bulk async copies (K and V; only the
+//   valid rows of a sequence's last block).
 // * Units of all sequences are laid end to end and every CTA of a persistent grid
-//   (num_SMs x resident CTAs) streams an equal contiguous share through an S-stage
-//   shared-memory ring whose stages complete on mbarriers.  Load balance is therefore
-//   independent of the context-length distribution.
-// * A sequence split across CTAs is merged by the last CTA to finish it (arrival
-//   counter + fences, no spinning): each CTA writes (m, l, acc) per head to a partial
-//   slot indexed (b + c); the last arrival combines them and resets the counter.
-// * Warp w owns heads [w*HPW, (w+1)*HPW).  Q·K: LPR = 32/block_size lanes per row,
-//   each lane keeping its share of q (pre-scaled by scale*log2 e) in registers, read in
-//   a per-row rotated chunk order so the 8 lanes of a shared-memory phase hit distinct
-//   banks.  Online softmax in base 2 with warp shuffles.  P·V: each lane owns D/32 dims.
+//   (num_SMs x resident CTAs) streams an equal contiguous share, so load balance does
+//   not depend on the context-length distribution.
+// * Warp specialisation: one producer warp (lane 0) runs ahead through an S-stage
+//   shared-memory ring (full mbarriers complete on the copies' bytes; empty mbarriers
+//   collect one arrival per compute warp), so compute warps never meet a CTA-wide
+//   barrier per unit.  Compute warp w owns heads [w*HPW, (w+1)*HPW).
+// * q·k: 32/block_size lanes per row, q (pre-scaled by scale*log2 e) in registers, K
+//   chunks read in a per-row rotated order so the 8 lanes of a shared-memory phase hit
+//   distinct banks.  p·v: each lane owns one 16-byte chunk of a row and the warp walks
+//   32/chunks_per_row rows at a time; partial sums across row groups are folded once per
+//   sequence.  Online softmax in base 2; packed fp32x2 FMAs throughout.
+// * A sequence split across CTAs is merged by the last CTA to finish it: each CTA writes
+//   (m, l, acc) per head to partial slot (b + c); after a CTA barrier one thread fences
+//   and bumps the sequence's arrival counter; the last arrival combines the partials
+//   and resets the counter (no spinning, no second launch).
 #include "spd_params.cuh"
 
 namespace spd {
 
+template <typename T>
+struct Pair;
+template <>
+struct Pair<float> {
+  static __device__ __forceinline__ float2 to_f2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+};
+template <>
+struct Pair<__half> {
+  static __device__ __forceinline__ float2 to_f2(const __half* p) {
+    return __half22float2(*reinterpret_cast<const __half2*>(p));
+  }
+};
+template <>
+struct Pair<__nv_bfloat16> {
+  static __device__ __forceinline__ float2 to_f2(const __nv_bfloat16* p) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+  }
+};
+
+// N consecutive elements (N even) -> N/2 float2, using the widest aligned vector load.
+template <typename T, int N>
+__device__ __forceinline__ void load_f2(const T* p, float2* out) {
+  constexpr int BYTES = N * (int)sizeof(T);
+  if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 16 / (int)sizeof(T)) {
+      const uint4 v = *reinterpret_cast<const uint4*>(p + i);
+      const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int k = 0; k < 16 / (int)sizeof(T); k += 2) out[(i + k) / 2] = Pair<T>::to_f2(e + k);
+    }
+  } else if constexpr (BYTES % 8 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 8 / (int)sizeof(T)) {
+      const uint2 v = *reinterpret_cast<const uint2*>(p + i);
+      const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int k = 0; k < 8 / (int)sizeof(T); k += 2) out[(i + k) / 2] = Pair<T>::to_f2(e + k);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; i += 2) out[i / 2] = Pair<T>::to_f2(p + i);
+  }
+}
+
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 template <typename T, int D, int BS>
 struct PagedGeom {
   static constexpr int EB = sizeof(T);
-  static constexpr int LPR = 32 / BS;                        // lanes per row for q·k
-  static constexpr int DPL = D / LPR;                        // dims per lane for q·k
-  static constexpr int CH = (DPL * EB >= 16) ? 16 / EB : DPL;  // elems per smem chunk
-  static constexpr int NCH = DPL / CH;                       // chunks per lane
-  static constexpr int PVL = D >= 32 ? 32 : D;               // lanes per row for p·v
-  static constexpr int PRG = 32 / PVL;                       // row groups for p·v
-  static constexpr int DPV = D / PVL;                        // dims per lane for p·v
-  static_assert(LPR >= 1 && LPR * BS == 32, "block_size must divide 32");
-  static_assert(DPL * LPR == D && DPV * PVL == D, "bad head_dim");
+  static constexpr int LPR = 32 / BS;                          // lanes per row for q·k
+  static constexpr int DPL = D / LPR;                          // dims per lane for q·k
+  static constexpr int CH = (DPL * EB >= 16) ? 16 / EB : DPL;  // elements per q·k chunk
+  static constexpr int NCH = DPL / CH;                         // chunks per lane
+  static constexpr int VE = 16 / EB;                           // elements per p·v chunk
+  static constexpr int CPR = D / VE;                           // p·v chunks per row
+  static constexpr int RG = 32 / CPR;                          // rows per p·v pass
+  static constexpr int PVP = (BS + RG - 1) / RG;               // p·v passes per block
+  static_assert(LPR * BS == 32 && DPL * LPR == D, "block_size must divide 32");
+  static_assert(CPR * VE == D && RG * CPR == 32, "head_dim / dtype combination");
+  static_assert((NCH & (NCH - 1)) == 0 && DPL % 2 == 0, "chunking");
 };
 
+constexpr int kPagedComputeBarrier = 1;  // named barrier among compute warps
+
 template <typename T, int D, int BS, int HPW>
-__global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParams p) {
+__global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParams p) {
   using Gm = PagedGeom<T, D, BS>;
   constexpr int LPR = Gm::LPR, DPL = Gm::DPL, CH = Gm::CH, NCH = Gm::NCH;
-  constexpr int PVL = Gm::PVL, PRG = Gm::PRG, DPV = Gm::DPV;
+  constexpr int VE = Gm::VE, CPR = Gm::CPR, RG = Gm::RG, PVP = Gm::PVP;
 
   extern __shared__ __align__(128) unsigned char smem[];
   const int H = p.H, B = p.B, S = p.stages;
   const int HD = H * D;
+  const int NW = (H + HPW - 1) / HPW;  // compute warps; warp NW is the producer
+  const int NCT = NW * 32;             // compute threads
   const size_t unit_elems = (size_t)BS * HD;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nthreads = blockDim.x;
 
   T* ring = reinterpret_cast<T*>(smem);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + round_up((size_t)S * 2 * unit_elems * sizeof(T), 128));
-  int* prefix = reinterpret_cast<int*>(bars + S);  // [B + 1] unit prefix over sequences
-  int* ctx_s = prefix + B + 1;                     // [B] clamped context lengths
-  int* flag = ctx_s + B;                           // [1] "this CTA finishes the sequence"
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + round_up((size_t)S * 2 * unit_elems * sizeof(T), 128));
+  uint64_t* empty = full + S;
+  int* prefix = reinterpret_cast<int*>(empty + S);  // [B + 1] unit prefix over sequences
+  int* ctx_s = prefix + B + 1;                      // [B] clamped context lengths
+  int* flag = ctx_s + B;                            // [0] last-arrival, [1] abort
 
   const T* __restrict__ kpool = reinterpret_cast<const T*>(p.k_pool);
   const T* __restrict__ vpool = reinterpret_cast<const T*>(p.v_pool);
@@ -69,7 +133,7 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
   const int max_ctx = p.max_blocks * BS;
 
   // ---- 1. unit prefix over sequences (every CTA computes it; B is small) ----------
-  for (int i = tid; i < B; i += nthreads) {
+  for (int i = tid; i < B; i += blockDim.x) {
     int c = p.context_lens[i];
     if (c > max_ctx) {
       set_error(p.err, SPD_DEVERR_LENGTH);
@@ -79,7 +143,10 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
     ctx_s[i] = c;
     prefix[i + 1] = (c + BS - 1) / BS;
   }
-  if (tid == 0) prefix[0] = 0;
+  if (tid == 0) {
+    prefix[0] = 0;
+    flag[1] = 0;
+  }
   __syncthreads();
   if (warp == 0) {
     int carry = 0;
@@ -99,69 +166,92 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
 
   const long long W = prefix[B];
   // Effective grid: never more CTAs than units, so every participating CTA owns at
-  // least one unit and the CTAs sharing a segment are consecutive (which the
-  // arrival count nparts = c_last - c_first + 1 relies on).
+  // least one unit and the CTAs sharing a sequence are consecutive (which the arrival
+  // count nparts = c_last - c_first + 1 relies on).
   const int c = blockIdx.x;
   const int G = (int)((long long)gridDim.x < W ? (long long)gridDim.x : W);
 
-  // ---- 2. sequences with nothing to attend to get zeros (CTA b % G) ---------------
+  // ---- 2. sequences with nothing to attend to get zeros (CTA b % gridDim) ----------
   for (int b = c; b < B; b += gridDim.x) {
     if (prefix[b + 1] == prefix[b]) {
-      for (int i = tid; i < HD; i += nthreads) out[(size_t)b * HD + i] = Elem<T>::from_f(0.f);
+      for (int i = tid; i < HD; i += blockDim.x) out[(size_t)b * HD + i] = Elem<T>::from_f(0.f);
     }
   }
   if (W == 0 || c >= G) return;
   const long long start = range_start(c, G, W), end = range_start(c + 1, G, W);
-  if (start >= end) return;
 
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NW);
+    }
     fence_barrier_init();
   }
   __syncthreads();
 
-  // ---- 3. producer (thread 0): issue unit u into stage (u - start) % S -------------
-  int pb = upper_index_i32(prefix, B, start);
-  long long issued = start;
-  auto issue = [&](long long u) {
-    while (prefix[pb + 1] <= u) ++pb;
-    const int j = (int)(u - prefix[pb]);
-    const int nvalid = min(BS, ctx_s[pb] - j * BS);
-    int phys = p.block_tables[(size_t)pb * p.max_blocks + j];
-    if (phys < 0 || phys >= p.num_blocks) {
-      set_error(p.err, SPD_DEVERR_BLOCK_ID);
-      phys = 0;
+  // ---- 3. producer warp -------------------------------------------------------------
+  if (warp == NW) {
+    if (lane == 0) {
+      int pb = upper_index_i32(prefix, B, start);
+      int s = 0;
+      uint32_t ph = 0;
+      long long issued = start;
+      for (long long u = start; u < end; ++u) {
+        if (u - start >= S) {
+          if (*((volatile int*)&flag[1]) || !mbar_wait_bounded(&empty[s], ph ^ 1, p.err)) {
+            flag[1] = 1;
+            break;
+          }
+        }
+        while (prefix[pb + 1] <= u) ++pb;
+        const int j = (int)(u - prefix[pb]);
+        const int nvalid = min(BS, ctx_s[pb] - j * BS);
+        int phys = p.block_tables[(size_t)pb * p.max_blocks + j];
+        if (phys < 0 || phys >= p.num_blocks) {
+          set_error(p.err, SPD_DEVERR_BLOCK_ID);
+          phys = 0;
+        }
+        const size_t off = (size_t)phys * unit_elems;
+        const uint32_t bytes = (uint32_t)(nvalid * HD * (int)sizeof(T));
+        T* dst = ring + (size_t)s * 2 * unit_elems;
+        mbar_arrive_expect_tx(&full[s], 2 * bytes);
+        bulk_copy_g2s(dst, kpool + off, bytes, &full[s]);
+        bulk_copy_g2s(dst + unit_elems, vpool + off, bytes, &full[s]);
+        issued = u + 1;
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      // Copies still in flight land before this CTA's shared memory is released:
+      // wait (bounded) for the last phase of every stage that was used.
+      const long long n = issued - start;
+      for (int k = 0; k < S && k < n; ++k) {
+        const long long u = issued - 1 - k;
+        const int st = (int)((u - start) % S);
+        (void)mbar_wait_bounded(&full[st], (uint32_t)(((u - start) / S) & 1), nullptr);
+      }
     }
-    const size_t off = (size_t)phys * unit_elems;
-    const uint32_t bytes = (uint32_t)(nvalid * HD * (int)sizeof(T));
-    const int s = (int)((u - start) % S);
-    T* dst = ring + (size_t)s * 2 * unit_elems;
-    mbar_arrive_expect_tx(&bars[s], 2 * bytes);
-    bulk_copy_g2s(dst, kpool + off, bytes, &bars[s]);
-    bulk_copy_g2s(dst + unit_elems, vpool + off, bytes, &bars[s]);
-  };
-  if (tid == 0) {
-    for (int k = 0; k < S && issued < end; ++k) issue(issued++);
+    return;
   }
 
-  // ---- 4. consumers ----------------------------------------------------------------
-  const int r = lane / LPR;    // row of this lane for q·k
+  // ---- 4. compute warps -----------------------------------------------------------------
+  const int r = lane / LPR;    // q·k row of this lane
   const int sub = lane % LPR;  // which DPL-slice of the row
-  const int rot = r % NCH;     // rotated chunk order (bank spreading)
-  const int dl = lane % PVL;   // p·v: dims [dl*DPV, dl*DPV + DPV)
-  const int rg = lane / PVL;   // p·v: row group
+  const int rot = r & (NCH - 1);
+  const int cidx = lane % CPR;  // p·v chunk of this lane
+  const int rg = lane / CPR;    // p·v row group
 
-  float qr[HPW][DPL];
-  float m[HPW], l[HPW], acc[HPW][DPV];
+  float2 qr[HPW][DPL / 2];
+  float m[HPW], l[HPW];
+  float2 acc[HPW][VE / 2];
 
   int b = upper_index_i32(prefix, B, start);
   bool need_q = true;
-  bool timed_out = false;
-  long long abort_at = -1;  // first unit not consumed when a wait ran out
+  int s = 0;
+  uint32_t ph = 0;
 
   for (long long g = start; g < end; ++g) {
-    const int s = (int)((g - start) % S);
-    const uint32_t parity = (uint32_t)(((g - start) / S) & 1);
     if (need_q) {
 #pragma unroll
       for (int k = 0; k < HPW; ++k) {
@@ -169,21 +259,26 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
         m[k] = -INFINITY;
         l[k] = 0.f;
 #pragma unroll
-        for (int i = 0; i < DPV; ++i) acc[k][i] = 0.f;
+        for (int i = 0; i < VE / 2; ++i) acc[k][i] = make_float2(0.f, 0.f);
         if (h < H) {
           const T* qrow = qg + ((size_t)b * H + h) * D + sub * DPL;
 #pragma unroll
           for (int cc = 0; cc < NCH; ++cc) {
-            const int ci = (cc + rot) % NCH;
+            const int ci = (cc + rot) & (NCH - 1);
+            load_f2<T, CH>(qrow + ci * CH, &qr[k][cc * CH / 2]);
 #pragma unroll
-            for (int e = 0; e < CH; ++e) qr[k][cc * CH + e] = Elem<T>::to_f(qrow[ci * CH + e]) * p.scale_log2;
+            for (int e = 0; e < CH / 2; ++e) {
+              qr[k][cc * CH / 2 + e].x *= p.scale_log2;
+              qr[k][cc * CH / 2 + e].y *= p.scale_log2;
+            }
           }
         }
       }
       need_q = false;
     }
 
-    const bool ok = mbar_wait_bounded(&bars[s], parity, p.err);
+    const bool ok = !*((volatile int*)&flag[1]) && mbar_wait_bounded(&full[s], ph, p.err);
+    if (!ok) flag[1] = 1;
     const int j = (int)(g - prefix[b]);
     const int nblk = prefix[b + 1] - prefix[b];
     const int nvalid = min(BS, ctx_s[b] - j * BS);
@@ -201,7 +296,7 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
       const T* vsrc = reinterpret_cast<const T*>(p.v_new) + (size_t)b * HD;
       constexpr int VEC = 16 / sizeof(T);
       if (ok) {
-        for (int i = tid * VEC; i < HD; i += nthreads * VEC) {
+        for (int i = tid * VEC; i < HD; i += NCT * VEC) {
           const uint4 kv = *reinterpret_cast<const uint4*>(ksrc + i);
           const uint4 vv = *reinterpret_cast<const uint4*>(vsrc + i);
           *reinterpret_cast<uint4*>(Ks + row_off + i) = kv;
@@ -210,8 +305,8 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
           *reinterpret_cast<uint4*>(vdst + i) = vv;
         }
       }
-      fence_proxy_async_smem();
-      __syncthreads();
+      fence_proxy_async_smem();  // generic writes before the next bulk copy into this stage
+      named_sync(kPagedComputeBarrier, NCT);
     }
 
     if (ok) {
@@ -221,55 +316,54 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
         if (h >= H) continue;
         const T* Kh = Ks + h * D;
         const T* Vh = Vs + h * D;
-        // q·k for row r (LPR lanes per row)
+        // q·k for row r
         float sc = -INFINITY;
         if (r < nvalid) {
           const T* krow = Kh + (size_t)r * HD + sub * DPL;
-          float dot = 0.f;
+          float2 dot = make_float2(0.f, 0.f);
 #pragma unroll
           for (int cc = 0; cc < NCH; ++cc) {
-            const int ci = (cc + rot) % NCH;
-            float kv[CH];
-            load_to_float<T, CH>(krow + ci * CH, kv);
+            const int ci = (cc + rot) & (NCH - 1);
+            float2 kv[CH / 2];
+            load_f2<T, CH>(krow + ci * CH, kv);
 #pragma unroll
-            for (int e = 0; e < CH; ++e) dot = fmaf(qr[k][cc * CH + e], kv[e], dot);
+            for (int e = 0; e < CH / 2; ++e) dot = __ffma2_rn(qr[k][cc * CH / 2 + e], kv[e], dot);
           }
-          sc = dot;
+          sc = dot.x + dot.y;
         }
 #pragma unroll
         for (int o = 1; o < LPR; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
         if (r >= nvalid) sc = -INFINITY;
-        const float mblk = warp_max(sc);
-        const float mnew = fmaxf(m[k], mblk);
+        const float mnew = fmaxf(m[k], warp_max(sc));
         const float alpha = exp2f(m[k] - mnew);
         const float pr = (r < nvalid) ? exp2f(sc - mnew) : 0.f;
         l[k] = l[k] * alpha + (sub == 0 ? pr : 0.f);
-#pragma unroll
-        for (int i = 0; i < DPV; ++i) acc[k][i] *= alpha;
         m[k] = mnew;
-        // p·v: row groups of PVL lanes walk the valid rows
-        for (int r0 = 0; r0 < nvalid; r0 += PRG) {
-          const int rr = r0 + rg;
-          const float prr = __shfl_sync(0xffffffffu, pr, min(rr, BS - 1) * LPR);
-          if (rr < nvalid) {
-            float vv[DPV];
-            load_to_float<T, DPV>(Vh + (size_t)rr * HD + dl * DPV, vv);
+        const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
-            for (int i = 0; i < DPV; ++i) acc[k][i] = fmaf(prr, vv[i], acc[k][i]);
+        for (int i = 0; i < VE / 2; ++i) acc[k][i] = __fmul2_rn(acc[k][i], a2);
+        // p·v: this lane's 16-byte chunk of rows rg, rg+RG, ...
+#pragma unroll
+        for (int ps = 0; ps < PVP; ++ps) {
+          const int rr = ps * RG + rg;
+          const float prr = __shfl_sync(0xffffffffu, pr, (rr < BS ? rr : 0) * LPR);
+          if (rr < nvalid) {
+            float2 vv[VE / 2];
+            load_f2<T, VE>(Vh + (size_t)rr * HD + cidx * VE, vv);
+            const float2 p2 = make_float2(prr, prr);
+#pragma unroll
+            for (int i = 0; i < VE / 2; ++i) acc[k][i] = __ffma2_rn(p2, vv[i], acc[k][i]);
           }
         }
       }
-    } else {
-      timed_out = true;
     }
-
-    // All warps are done with stage s: refill it.  The OR makes the abort decision
-    // uniform across the CTA.
-    if (__syncthreads_or(timed_out)) {
-      abort_at = g;
-      break;
+    // this warp is done with stage s
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (++s == S) {
+      s = 0;
+      ph ^= 1;
     }
-    if (tid == 0 && issued < end) issue(issued++);
 
     // ---- segment end: finish sequence b -------------------------------------------
     const bool seq_end = (g + 1 == prefix[b + 1]);
@@ -279,12 +373,13 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
 #pragma unroll
       for (int k = 0; k < HPW; ++k) {
         ltot[k] = warp_sum(l[k]);
-        if constexpr (PRG > 1) {
 #pragma unroll
-          for (int o = PVL; o < 32; o <<= 1)
+        for (int o = CPR; o < 32; o <<= 1)
 #pragma unroll
-            for (int i = 0; i < DPV; ++i) acc[k][i] += __shfl_xor_sync(0xffffffffu, acc[k][i], o);
-        }
+          for (int i = 0; i < VE / 2; ++i) {
+            acc[k][i].x += __shfl_xor_sync(0xffffffffu, acc[k][i].x, o);
+            acc[k][i].y += __shfl_xor_sync(0xffffffffu, acc[k][i].y, o);
+          }
       }
       if (whole) {
 #pragma unroll
@@ -292,9 +387,12 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
           const int h = warp * HPW + k;
           if (h < H && rg == 0) {
             const float inv = 1.f / ltot[k];
-            T* o = out + ((size_t)b * H + h) * D + dl * DPV;
+            T* o = out + ((size_t)b * H + h) * D + cidx * VE;
 #pragma unroll
-            for (int i = 0; i < DPV; ++i) o[i] = Elem<T>::from_f(acc[k][i] * inv);
+            for (int i = 0; i < VE / 2; ++i) {
+              o[2 * i] = Elem<T>::from_f(acc[k][i].x * inv);
+              o[2 * i + 1] = Elem<T>::from_f(acc[k][i].y * inv);
+            }
           }
         }
       } else {
@@ -309,7 +407,8 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
             float* slot = p.partials + ((size_t)(b + c) * H + h) * (D + 2);
             if (rg == 0) {
 #pragma unroll
-              for (int i = 0; i < DPV; ++i) slot[dl * DPV + i] = acc[k][i];
+              for (int i = 0; i < VE / 2; ++i)
+                *reinterpret_cast<float2*>(slot + cidx * VE + 2 * i) = acc[k][i];
             }
             if (lane == 0) {
               slot[D] = m[k];
@@ -317,36 +416,45 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
             }
           }
         }
-        __threadfence();
-        __syncthreads();
+        // every compute thread's partial writes precede thread 0's fence + arrival
+        named_sync(kPagedComputeBarrier, NCT);
         if (tid == 0) {
+          __threadfence();
           const int old = atomicAdd(&p.counters[b], 1);
           const int last = (old == nparts - 1);
-          if (last) p.counters[b] = 0;  // every part has arrived; ready for the next call
-          *flag = last;
+          if (last) {
+            p.counters[b] = 0;  // every part has arrived; ready for the next call
+            __threadfence();
+          }
+          flag[0] = last;
         }
-        __syncthreads();
-        if (*flag) {
-          __threadfence();
-          for (int h = warp; h < H; h += nthreads / 32) {
+        named_sync(kPagedComputeBarrier, NCT);
+        if (flag[0]) {
+          for (int h = warp; h < H; h += NW) {
             float M = -INFINITY;
             for (int cc = c_first; cc <= c_last; ++cc)
               M = fmaxf(M, __ldcg(p.partials + ((size_t)(b + cc) * H + h) * (D + 2) + D));
-            float L = 0.f, o[DPV];
+            float L = 0.f;
+            float2 o[VE / 2];
 #pragma unroll
-            for (int i = 0; i < DPV; ++i) o[i] = 0.f;
+            for (int i = 0; i < VE / 2; ++i) o[i] = make_float2(0.f, 0.f);
             for (int cc = c_first; cc <= c_last; ++cc) {
               const float* slot = p.partials + ((size_t)(b + cc) * H + h) * (D + 2);
               const float w = exp2f(__ldcg(slot + D) - M);
               L = fmaf(__ldcg(slot + D + 1), w, L);
+              const float2 w2 = make_float2(w, w);
 #pragma unroll
-              for (int i = 0; i < DPV; ++i) o[i] = fmaf(__ldcg(slot + dl * DPV + i), w, o[i]);
+              for (int i = 0; i < VE / 2; ++i)
+                o[i] = __ffma2_rn(__ldcg(reinterpret_cast<const float2*>(slot + cidx * VE + 2 * i)), w2, o[i]);
             }
             if (rg == 0) {
               const float inv = 1.f / L;
-              T* op = out + ((size_t)b * H + h) * D + dl * DPV;
+              T* op = out + ((size_t)b * H + h) * D + cidx * VE;
 #pragma unroll
-              for (int i = 0; i < DPV; ++i) op[i] = Elem<T>::from_f(o[i] * inv);
+              for (int i = 0; i < VE / 2; ++i) {
+                op[2 * i] = Elem<T>::from_f(o[i].x * inv);
+                op[2 * i + 1] = Elem<T>::from_f(o[i].y * inv);
+              }
             }
           }
         }
@@ -358,13 +466,6 @@ __global__ void __launch_bounds__(512) paged_decode_attn_kernel(const PagedParam
       }
     }
   }
-
-  if (abort_at >= 0 && tid == 0) {
-    // A copy never completed: wait (bounded) for the copies still in flight, then leave.
-    for (long long u = abort_at; u < issued; ++u) {
-      (void)mbar_wait_bounded(&bars[(u - start) % S], (uint32_t)(((u - start) / S) & 1), nullptr);
-    }
-  }
 }
 
 // ------------------------------------------------------------------ host launcher
@@ -372,26 +473,25 @@ template <typename T, int D, int BS, int HPW>
 static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t stream) {
   PagedParams p = base;
   const int nw = (p.H + HPW - 1) / HPW;
-  const int threads = nw * 32;
+  const int threads = (nw + 1) * 32;
   const size_t stage_bytes = (size_t)2 * BS * p.H * D * sizeof(T);
-  // Ring depth: enough stages for ~96 KB in flight, at least two when two fit.
-  int S = (int)((96 * 1024) / stage_bytes);
+  // Ring depth: up to ~200 KB of copies in flight per CTA (one CTA per SM at the
+  // Whisper shapes; the producer warp keeps every stage busy), at least two stages.
+  int S = (int)((200 * 1024) / stage_bytes);
   if (S < 2 && 2 * stage_bytes <= 200 * 1024) S = 2;
   S = S < 1 ? 1 : (S > 8 ? 8 : S);
   p.stages = S;
-  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 8 * (size_t)S + 4 * (2 * (size_t)p.B + 2);
+  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * (size_t)S + 4 * (2 * (size_t)p.B + 3);
   if (smem > 227 * 1024) return SPD_ERR_UNSUPPORTED;
   auto kfn = paged_decode_attn_kernel<T, D, BS, HPW>;
-  if (smem > 48 * 1024) {
-    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return SPD_ERR_CUDA;
-  }
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return SPD_ERR_CUDA;
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kfn, threads, smem) != cudaSuccess || occ < 1)
     return SPD_ERR_CUDA;
   if (occ > kMaxCtasPerSm) occ = kMaxCtasPerSm;
-  const int grid = device_sms * occ;
-  kfn<<<grid, threads, smem, stream>>>(p);
+  kfn<<<device_sms * occ, threads, smem, stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? SPD_OK : SPD_ERR_CUDA;
 }
 
