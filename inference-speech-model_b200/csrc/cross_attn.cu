@@ -17,6 +17,16 @@
 
 namespace spd {
 
+constexpr int kCrossComputeBarrier = 1;  // named barrier among compute warps
+
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 template <typename T, int D>
 struct CrossGeom {
   static constexpr int EB = sizeof(T);
@@ -34,24 +44,27 @@ struct CrossGeom {
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
+__global__ void __launch_bounds__(288) cross_attn_kernel(const CrossParams p) {
   using Gm = CrossGeom<T, D>;
   constexpr int NW = Gm::NW, LPR = Gm::LPR, RPP = Gm::RPP, DPL = Gm::DPL, CH = Gm::CH;
   constexpr int NCH = Gm::NCH, PASSES = Gm::PASSES, C = Gm::C;
   constexpr int PVL = Gm::PVL, PRG = Gm::PRG, DPV = Gm::DPV;
+  constexpr int NCT = NW * 32;  // compute threads; warp NW is the producer
 
   extern __shared__ __align__(128) unsigned char smem[];
   const int H = p.H, B = p.B, S = p.stages;
   const size_t unit_elems = (size_t)C * D;
+  const size_t stage_elems = 2 * unit_elems + D;  // K chunk, V chunk, q row
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   T* ring = reinterpret_cast<T*>(smem);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + round_up((size_t)S * 2 * unit_elems * sizeof(T), 128));
-  float* merge = reinterpret_cast<float*>(bars + S);  // [NW][D + 2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + round_up((size_t)S * stage_elems * sizeof(T), 128));
+  uint64_t* empty = full + S;
+  float* merge = reinterpret_cast<float*>(empty + S);          // [NW][D + 2]
   int* prefix = reinterpret_cast<int*>(merge + NW * (D + 2));  // [B + 1], units * H
   int* nch_s = prefix + B + 1;                                 // [B] chunks per pair
   int* val_s = nch_s + B;                                      // [B] clamped valid length
-  int* flag = val_s + B;
+  int* flag = val_s + B;                                       // [0] last-arrival, [1] abort
 
   const T* __restrict__ kg = reinterpret_cast<const T*>(p.k);
   const T* __restrict__ vg = reinterpret_cast<const T*>(p.v);
@@ -70,7 +83,10 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
     nch_s[i] = (v + C - 1) / C;
     prefix[i + 1] = nch_s[i] * H;
   }
-  if (tid == 0) prefix[0] = 0;
+  if (tid == 0) {
+    prefix[0] = 0;
+    flag[1] = 0;
+  }
   __syncthreads();
   if (warp == 0) {
     int carry = 0;
@@ -89,9 +105,7 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
   __syncthreads();
 
   const long long W = prefix[B];
-  // Effective grid: never more CTAs than units, so every participating CTA owns at
-  // least one unit and the CTAs sharing a segment are consecutive (which the
-  // arrival count nparts = c_last - c_first + 1 relies on).
+  // Effective grid: never more CTAs than units (see paged_decode_attn.cu).
   const int c = blockIdx.x;
   const int G = (int)((long long)gridDim.x < W ? (long long)gridDim.x : W);
   for (int b = c; b < B; b += gridDim.x) {
@@ -101,35 +115,59 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
   }
   if (W == 0 || c >= G) return;
   const long long start = range_start(c, G, W), end = range_start(c + 1, G, W);
-  if (start >= end) return;
 
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NW);
+    }
     fence_barrier_init();
   }
   __syncthreads();
 
-  // ---- producer ----------------------------------------------------------------------
-  int pb = upper_index_i32(prefix, B, start);
-  long long issued = start;
-  auto issue = [&](long long u) {
-    while (prefix[pb + 1] <= u) ++pb;
-    const int off = (int)(u - prefix[pb]);
-    const int h = off / nch_s[pb], j = off % nch_s[pb];
-    const int nrows = min(C, val_s[pb] - j * C);
-    const size_t src = (size_t)pb * p.kv_batch_stride + (size_t)h * p.kv_head_stride + (size_t)j * C * D;
-    const uint32_t bytes = (uint32_t)(nrows * D * (int)sizeof(T));
-    const int s = (int)((u - start) % S);
-    T* dst = ring + (size_t)s * 2 * unit_elems;
-    mbar_arrive_expect_tx(&bars[s], 2 * bytes);
-    bulk_copy_g2s(dst, kg + src, bytes, &bars[s]);
-    bulk_copy_g2s(dst + unit_elems, vg + src, bytes, &bars[s]);
-  };
-  if (tid == 0) {
-    for (int k = 0; k < S && issued < end; ++k) issue(issued++);
+  // ---- producer warp ---------------------------------------------------------------
+  if (warp == NW) {
+    if (lane == 0) {
+      int pb = upper_index_i32(prefix, B, start);
+      int s = 0;
+      uint32_t ph = 0;
+      long long issued = start;
+      for (long long u = start; u < end; ++u) {
+        if (u - start >= S) {
+          if (*((volatile int*)&flag[1]) || !mbar_wait_bounded(&empty[s], ph ^ 1, p.err)) {
+            flag[1] = 1;
+            break;
+          }
+        }
+        while (prefix[pb + 1] <= u) ++pb;
+        const int off = (int)(u - prefix[pb]);
+        const int h = off / nch_s[pb], j = off % nch_s[pb];
+        const int nrows = min(C, val_s[pb] - j * C);
+        const size_t src = (size_t)pb * p.kv_batch_stride + (size_t)h * p.kv_head_stride + (size_t)j * C * D;
+        const uint32_t bytes = (uint32_t)(nrows * D * (int)sizeof(T));
+        const bool seg_first = (u == start) || (j == 0);
+        const uint32_t qbytes = seg_first ? (uint32_t)(D * sizeof(T)) : 0u;
+        T* dst = ring + (size_t)s * stage_elems;
+        mbar_arrive_expect_tx(&full[s], 2 * bytes + qbytes);
+        bulk_copy_g2s(dst, kg + src, bytes, &full[s]);
+        bulk_copy_g2s(dst + unit_elems, vg + src, bytes, &full[s]);
+        if (seg_first) bulk_copy_g2s(dst + 2 * unit_elems, qg + ((size_t)pb * H + h) * D, qbytes, &full[s]);
+        issued = u + 1;
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      const long long n = issued - start;
+      for (int k = 0; k < S && k < n; ++k) {
+        const long long u = issued - 1 - k;
+        (void)mbar_wait_bounded(&full[(u - start) % S], (uint32_t)(((u - start) / S) & 1), nullptr);
+      }
+    }
+    return;
   }
 
-  // ---- consumers ---------------------------------------------------------------------
+  // ---- compute warps -----------------------------------------------------------------
   const int r = lane / LPR, sub = lane % LPR, rot = r % NCH;
   const int dl = lane % PVL, rg = lane / PVL;
   float qr[DPL];
@@ -138,32 +176,31 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
   int b = upper_index_i32(prefix, B, start);
   int h = (int)((start - prefix[b]) / nch_s[b]);
   bool need_q = true;
-  bool timed_out = false;
-  long long abort_at = -1;
+  int s = 0;
+  uint32_t ph = 0;
 
   for (long long g = start; g < end; ++g) {
-    const int s = (int)((g - start) % S);
-    const uint32_t parity = (uint32_t)(((g - start) / S) & 1);
+    const bool ok = !*((volatile int*)&flag[1]) && mbar_wait_bounded(&full[s], ph, p.err);
+    if (!ok) flag[1] = 1;
     const int off = (int)(g - prefix[b]);
     const int j = off % nch_s[b];
+    const int nrows = min(C, val_s[b] - j * C);
+    const T* Ks = ring + (size_t)s * stage_elems;
+    const T* Vs = Ks + unit_elems;
     if (need_q) {
       m = -INFINITY;
       l = 0.f;
 #pragma unroll
       for (int i = 0; i < DPV; ++i) acc[i] = 0.f;
-      const T* qrow = qg + ((size_t)b * H + h) * D + sub * DPL;
+      const T* qrow = Vs + unit_elems + sub * DPL;  // q row arrived with this unit
 #pragma unroll
       for (int cc = 0; cc < NCH; ++cc) {
         const int ci = (cc + rot) % NCH;
 #pragma unroll
-        for (int e = 0; e < CH; ++e) qr[cc * CH + e] = Elem<T>::to_f(qrow[ci * CH + e]) * p.scale_log2;
+        for (int e = 0; e < CH; ++e) qr[cc * CH + e] = ok ? Elem<T>::to_f(qrow[ci * CH + e]) * p.scale_log2 : 0.f;
       }
       need_q = false;
     }
-    const bool ok = mbar_wait_bounded(&bars[s], parity, p.err);
-    const int nrows = min(C, val_s[b] - j * C);
-    const T* Ks = ring + (size_t)s * 2 * unit_elems;
-    const T* Vs = Ks + unit_elems;
     if (ok) {
 #pragma unroll
       for (int ps = 0; ps < PASSES; ++ps) {
@@ -187,8 +224,7 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
 #pragma unroll
         for (int o = 1; o < LPR; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
         if (r >= nv) sc = -INFINITY;
-        const float mblk = warp_max(sc);
-        const float mnew = fmaxf(m, mblk);
+        const float mnew = fmaxf(m, warp_max(sc));
         const float alpha = exp2f(m - mnew);
         const float pr = (r < nv) ? exp2f(sc - mnew) : 0.f;
         l = l * alpha + (sub == 0 ? pr : 0.f);
@@ -206,18 +242,17 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
           }
         }
       }
-    } else {
-      timed_out = true;
     }
-    if (__syncthreads_or(timed_out)) {
-      abort_at = g;
-      break;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (++s == S) {
+      s = 0;
+      ph ^= 1;
     }
-    if (tid == 0 && issued < end) issue(issued++);
 
     const bool seg_end = (j == nch_s[b] - 1);
     if (seg_end || g + 1 == end) {
-      // merge the warps' states for pair (b, h)
+      // merge the compute warps' states for pair (b, h)
       float lw = warp_sum(l);
       if constexpr (PRG > 1) {
 #pragma unroll
@@ -234,12 +269,11 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
         mw[D] = m;
         mw[D + 1] = lw;
       }
-      __syncthreads();
+      named_sync(kCrossComputeBarrier, NCT);
       const long long pair = (long long)b * H + h;
       const long long u0 = prefix[b] + (long long)h * nch_s[b];
       const long long u1 = u0 + nch_s[b];
       const bool whole = (start <= u0) && (end >= u1);
-      // warp 0 merges: lane covers dims dl*DPV..
       float M = -INFINITY;
 #pragma unroll
       for (int w = 0; w < NW; ++w) M = fmaxf(M, merge[w * (D + 2) + D]);
@@ -276,17 +310,19 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
             slot[D + 1] = L;
           }
         }
-        __threadfence();
-        __syncthreads();
+        named_sync(kCrossComputeBarrier, NCT);
         if (tid == 0) {
+          __threadfence();
           const int old = atomicAdd(&p.counters[pair], 1);
           const int last = (old == nparts - 1);
-          if (last) p.counters[pair] = 0;
-          *flag = last;
+          if (last) {
+            p.counters[pair] = 0;
+            __threadfence();
+          }
+          flag[0] = last;
         }
-        __syncthreads();
-        if (*flag && warp == 0) {
-          __threadfence();
+        named_sync(kCrossComputeBarrier, NCT);
+        if (flag[0] && warp == 0) {
           float M2 = -INFINITY;
           for (int cc = c_first; cc <= c_last; ++cc)
             M2 = fmaxf(M2, __ldcg(p.partials + (size_t)(pair + cc) * (D + 2) + D));
@@ -308,7 +344,7 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
           }
         }
       }
-      __syncthreads();  // merge buffer is reused by the next pair
+      named_sync(kCrossComputeBarrier, NCT);  // merge buffer is reused by the next pair
       if (seg_end) {
         ++h;
         if (h == H) {
@@ -320,31 +356,26 @@ __global__ void __launch_bounds__(256) cross_attn_kernel(const CrossParams p) {
       }
     }
   }
-
-  if (abort_at >= 0 && tid == 0) {
-    for (long long u = abort_at; u < issued; ++u) {
-      (void)mbar_wait_bounded(&bars[(u - start) % S], (uint32_t)(((u - start) / S) & 1), nullptr);
-    }
-  }
 }
 
 template <typename T, int D>
 static int launch_cross(const CrossParams& base, int sms, cudaStream_t stream) {
   using Gm = CrossGeom<T, D>;
   CrossParams p = base;
-  const size_t stage_bytes = (size_t)2 * Gm::C * D * sizeof(T);
+  const size_t stage_bytes = ((size_t)2 * Gm::C + 1) * D * sizeof(T);
+  // ~96 KB of stages per CTA: two CTAs per SM, each with a producer warp streaming.
   int S = (int)((96 * 1024) / stage_bytes);
   S = S < 2 ? 2 : (S > 8 ? 8 : S);
   p.stages = S;
-  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 8 * (size_t)S +
-                      4 * (size_t)Gm::NW * (D + 2) + 4 * (3 * (size_t)p.B + 2);
+  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * (size_t)S +
+                      4 * (size_t)Gm::NW * (D + 2) + 4 * (3 * (size_t)p.B + 3);
   if (smem > 227 * 1024) return SPD_ERR_UNSUPPORTED;
   auto kfn = cross_attn_kernel<T, D>;
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return SPD_ERR_CUDA;
   int occ = 0;
-  const int threads = Gm::NW * 32;
+  const int threads = (Gm::NW + 1) * 32;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kfn, threads, smem) != cudaSuccess || occ < 1)
     return SPD_ERR_CUDA;
   if (occ > kMaxCtasPerSm) occ = kMaxCtasPerSm;

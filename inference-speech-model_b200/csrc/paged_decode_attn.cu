@@ -103,6 +103,7 @@ struct PagedGeom {
 };
 
 constexpr int kPagedComputeBarrier = 1;  // named barrier among compute warps
+constexpr int kIdsWindow = 256;          // block ids preloaded per CTA
 
 template <typename T, int D, int BS, int HPW>
 __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParams p) {
@@ -118,12 +119,15 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
   const size_t unit_elems = (size_t)BS * HD;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
+  // Stage s: K block, V block, then q / k_new / v_new rows of the unit's sequence.
+  const size_t stage_elems = 2 * unit_elems + 3 * (size_t)HD;
   T* ring = reinterpret_cast<T*>(smem);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + round_up((size_t)S * 2 * unit_elems * sizeof(T), 128));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + round_up((size_t)S * stage_elems * sizeof(T), 128));
   uint64_t* empty = full + S;
   int* prefix = reinterpret_cast<int*>(empty + S);  // [B + 1] unit prefix over sequences
   int* ctx_s = prefix + B + 1;                      // [B] clamped context lengths
   int* flag = ctx_s + B;                            // [0] last-arrival, [1] abort
+  int* ids = flag + 2;                              // [kIdsWindow] block ids of this CTA's units
 
   const T* __restrict__ kpool = reinterpret_cast<const T*>(p.k_pool);
   const T* __restrict__ vpool = reinterpret_cast<const T*>(p.v_pool);
@@ -187,6 +191,21 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
     }
     fence_barrier_init();
   }
+  // Block ids of the first kIdsWindow units of this CTA, loaded in parallel (one round
+  // trip) so the producer never waits on a block-table load.
+  {
+    const long long nids = min(end - start, (long long)kIdsWindow);
+    for (long long i = tid; i < nids; i += blockDim.x) {
+      const long long u = start + i;
+      const int bb = upper_index_i32(prefix, B, u);
+      int phys = p.block_tables[(size_t)bb * p.max_blocks + (u - prefix[bb])];
+      if (phys < 0 || phys >= p.num_blocks) {
+        set_error(p.err, SPD_DEVERR_BLOCK_ID);
+        phys = 0;
+      }
+      ids[i] = phys;
+    }
+  }
   __syncthreads();
 
   // ---- 3. producer warp -------------------------------------------------------------
@@ -206,17 +225,32 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
         while (prefix[pb + 1] <= u) ++pb;
         const int j = (int)(u - prefix[pb]);
         const int nvalid = min(BS, ctx_s[pb] - j * BS);
-        int phys = p.block_tables[(size_t)pb * p.max_blocks + j];
-        if (phys < 0 || phys >= p.num_blocks) {
-          set_error(p.err, SPD_DEVERR_BLOCK_ID);
-          phys = 0;
+        int phys;
+        if (u - start < kIdsWindow) {
+          phys = ids[u - start];
+        } else {
+          phys = p.block_tables[(size_t)pb * p.max_blocks + j];
+          if (phys < 0 || phys >= p.num_blocks) {
+            set_error(p.err, SPD_DEVERR_BLOCK_ID);
+            phys = 0;
+          }
         }
         const size_t off = (size_t)phys * unit_elems;
         const uint32_t bytes = (uint32_t)(nvalid * HD * (int)sizeof(T));
-        T* dst = ring + (size_t)s * 2 * unit_elems;
-        mbar_arrive_expect_tx(&full[s], 2 * bytes);
+        const uint32_t row_bytes = (uint32_t)(HD * (int)sizeof(T));
+        const bool seg_first = (u == start) || (u == prefix[pb]);
+        const bool app = append && (j == prefix[pb + 1] - prefix[pb] - 1);
+        T* dst = ring + (size_t)s * stage_elems;
+        mbar_arrive_expect_tx(&full[s], 2 * bytes + (seg_first ? row_bytes : 0u) + (app ? 2 * row_bytes : 0u));
         bulk_copy_g2s(dst, kpool + off, bytes, &full[s]);
         bulk_copy_g2s(dst + unit_elems, vpool + off, bytes, &full[s]);
+        if (seg_first) bulk_copy_g2s(dst + 2 * unit_elems, qg + (size_t)pb * HD, row_bytes, &full[s]);
+        if (app) {
+          bulk_copy_g2s(dst + 2 * unit_elems + HD, reinterpret_cast<const T*>(p.k_new) + (size_t)pb * HD, row_bytes,
+                        &full[s]);
+          bulk_copy_g2s(dst + 2 * unit_elems + 2 * HD, reinterpret_cast<const T*>(p.v_new) + (size_t)pb * HD,
+                        row_bytes, &full[s]);
+        }
         issued = u + 1;
         if (++s == S) {
           s = 0;
@@ -252,6 +286,15 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
   uint32_t ph = 0;
 
   for (long long g = start; g < end; ++g) {
+    const bool ok = !*((volatile int*)&flag[1]) && mbar_wait_bounded(&full[s], ph, p.err);
+    if (!ok) flag[1] = 1;
+    const int j = (int)(g - prefix[b]);
+    const int nblk = prefix[b + 1] - prefix[b];
+    const int nvalid = min(BS, ctx_s[b] - j * BS);
+    T* Ks = ring + (size_t)s * stage_elems;
+    T* Vs = Ks + unit_elems;
+    const T* Qs = Vs + unit_elems;  // q row of sequence b (first unit of a segment only)
+
     if (need_q) {
 #pragma unroll
       for (int k = 0; k < HPW; ++k) {
@@ -260,8 +303,8 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
         l[k] = 0.f;
 #pragma unroll
         for (int i = 0; i < VE / 2; ++i) acc[k][i] = make_float2(0.f, 0.f);
-        if (h < H) {
-          const T* qrow = qg + ((size_t)b * H + h) * D + sub * DPL;
+        if (h < H && ok) {
+          const T* qrow = Qs + h * D + sub * DPL;
 #pragma unroll
           for (int cc = 0; cc < NCH; ++cc) {
             const int ci = (cc + rot) & (NCH - 1);
@@ -277,14 +320,6 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
       need_q = false;
     }
 
-    const bool ok = !*((volatile int*)&flag[1]) && mbar_wait_bounded(&full[s], ph, p.err);
-    if (!ok) flag[1] = 1;
-    const int j = (int)(g - prefix[b]);
-    const int nblk = prefix[b + 1] - prefix[b];
-    const int nvalid = min(BS, ctx_s[b] - j * BS);
-    T* Ks = ring + (size_t)s * 2 * unit_elems;
-    T* Vs = Ks + unit_elems;
-
     if (append && j == nblk - 1) {
       // op (3) fused: the new token sits at row nvalid-1 of the sequence's last block.
       int phys = p.block_tables[(size_t)b * p.max_blocks + j];
@@ -292,8 +327,8 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
       const size_t row_off = (size_t)(nvalid - 1) * HD;
       T* kdst = const_cast<T*>(kpool) + (size_t)phys * unit_elems + row_off;
       T* vdst = const_cast<T*>(vpool) + (size_t)phys * unit_elems + row_off;
-      const T* ksrc = reinterpret_cast<const T*>(p.k_new) + (size_t)b * HD;
-      const T* vsrc = reinterpret_cast<const T*>(p.v_new) + (size_t)b * HD;
+      const T* ksrc = Qs + HD;  // k_new / v_new rows arrived with this unit
+      const T* vsrc = Qs + 2 * HD;
       constexpr int VEC = 16 / sizeof(T);
       if (ok) {
         for (int i = tid * VEC; i < HD; i += NCT * VEC) {
@@ -474,14 +509,16 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
   PagedParams p = base;
   const int nw = (p.H + HPW - 1) / HPW;
   const int threads = (nw + 1) * 32;
-  const size_t stage_bytes = (size_t)2 * BS * p.H * D * sizeof(T);
-  // Ring depth: up to ~200 KB of copies in flight per CTA (one CTA per SM at the
-  // Whisper shapes; the producer warp keeps every stage busy), at least two stages.
-  int S = (int)((200 * 1024) / stage_bytes);
-  if (S < 2 && 2 * stage_bytes <= 200 * 1024) S = 2;
+  const size_t stage_bytes = ((size_t)2 * BS + 3) * p.H * D * sizeof(T);
+  // Ring depth: up to ~216 KB of stages per CTA (one CTA per SM at the Whisper shapes;
+  // the producer warp keeps every stage in flight), at least two stages.
+  const size_t fixed = 16 * 8 + 4 * (2 * (size_t)p.B + 3 + kIdsWindow) + 256;
+  int S = (int)((216 * 1024 - fixed) / stage_bytes);
+  if (S < 2 && 2 * stage_bytes + fixed <= 227 * 1024) S = 2;
   S = S < 1 ? 1 : (S > 8 ? 8 : S);
   p.stages = S;
-  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * (size_t)S + 4 * (2 * (size_t)p.B + 3);
+  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * (size_t)S +
+                      4 * (2 * (size_t)p.B + 3 + kIdsWindow);
   if (smem > 227 * 1024) return SPD_ERR_UNSUPPORTED;
   auto kfn = paged_decode_attn_kernel<T, D, BS, HPW>;
   if (smem > 48 * 1024 &&
