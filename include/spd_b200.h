@@ -154,6 +154,29 @@ int spd_cross_kv_project(const void* enc_out, const void* w_kv, const void* b_kv
                          int D, int T_out, int64_t out_slot_stride, int dtype,
                          int32_t* error_word, void* stream);
 
+/* Allocation-free variant of spd_paged_decode_attn, for callers that cannot allocate
+ * GPU memory or own a workspace: code running where cudaMalloc is unavailable or
+ * forbidden (inside an allocator callback, a plugin host that hands out only the
+ * tensors of the call, a process whose memory budget is fixed up front).  It has no
+ * counterpart in the reference, which always allocates through PyTorch.
+ *   Same arguments and results as spd_paged_decode_attn, minus the workspace; the
+ *   split-KV scratch lives in a 4 MiB array inside the library that every GPU using this
+ *   entry point keeps until the process exits (SPD_NOALLOC_SCRATCH_BYTES).  Calls whose
+ *   spd_paged_decode_attn_workspace_size(B, H, D, device) exceeds it are rejected with
+ *   SPD_ERR_WORKSPACE (e.g. B=64, H=12, D=64 needs about 2.1 MiB on a 148-SM B200).
+ *   error_word: optional int32 device word that receives this call's SPD_DEVERR_* flags.
+ *   The first call on each device looks up the array's device address; make that first
+ *   call before capturing any stream.  Every call clears the scratch counters it needs,
+ *   and all calls share one array: calls that overlap on the GPU (different streams, or
+ *   several host threads) race and give wrong results. */
+#define SPD_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u)
+int spd_paged_decode_attn_noalloc(const void* q, void* k_pool, void* v_pool,
+                                  const int32_t* block_tables, const int32_t* context_lens,
+                                  void* out, int B, int H, int D, int block_size,
+                                  int max_blocks, int num_blocks, float scale, int dtype,
+                                  const void* k_new, const void* v_new, int32_t* error_word,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

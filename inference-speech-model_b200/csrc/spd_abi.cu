@@ -73,6 +73,12 @@ bool head_dim_ok(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
 
 }  // namespace
 
+namespace spd {
+// Records a host-side error for spd_get_last_error() from other translation units of
+// the library; returns `code`.
+int record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace spd
+
 extern "C" {
 
 int spd_version(void) { return 100; }
