@@ -205,7 +205,7 @@ def run_ours(args):
     c = CFG2
     sets = [make_inputs(1000 + 97 * rank + i, device=dev) for i in range(N_SETS)]
     outs = [torch.empty(c["B"], c["H"], c["D"], dtype=torch.float16, device=dev) for _ in range(N_SETS)]
-    ws = ops.paged_attn_workspace(c["B"], c["H"], c["D"], dev)
+    ws = ops.paged_attn_workspace(c["B"], c["H"], c["D"], sets[0]["tables"].shape[1], dev)
     bytes_per = [algorithmic_bytes(s["ctx"].cpu()) for s in sets]
 
     def launch(i):

@@ -69,13 +69,13 @@ int spd_version(void);
 int spd_get_last_error(char* buf, size_t size);
 
 /* Number of bytes of workspace the attention kernels need.  The workspace holds a
- * 256-byte header (device error word at offset 0), per-sequence arrival counters and
+ * 256-byte header (device error word at offset 0, work counters), arrival counters and
  * fp32 split-KV partial results.  It must be zero-filled once before first use; the
  * kernels leave every counter back at zero, so it can be reused by later calls with the
- * same (B, H, D) on the same stream.  A workspace used with another geometry must be
+ * same geometry on the same stream.  A workspace used with another geometry must be
  * zero-filled again first; calls that overlap on the GPU must use separate workspaces.
  * `device` < 0 means the current device. */
-size_t spd_paged_decode_attn_workspace_size(int B, int H, int D, int device);
+size_t spd_paged_decode_attn_workspace_size(int B, int H, int D, int max_blocks, int device);
 size_t spd_cross_attn_workspace_size(int B, int H, int D, int device);
 
 /* Copies the device error word of a workspace (or any int32 error word) to *host_word.
@@ -163,7 +163,7 @@ int spd_cross_kv_project(const void* enc_out, const void* w_kv, const void* b_kv
  *   split-KV scratch lives in a 4 MiB array inside the library that every GPU using this
  *   entry point keeps until the process exits (SPD_NOALLOC_SCRATCH_BYTES).  Calls whose
  *   spd_paged_decode_attn_workspace_size(B, H, D, device) exceeds it are rejected with
- *   SPD_ERR_WORKSPACE (e.g. B=64, H=12, D=64 needs about 2.1 MiB on a 148-SM B200).
+ *   SPD_ERR_WORKSPACE (e.g. B=64, H=12, D=64, 28 blocks per table needs about 2.9 MiB).
  *   error_word: optional int32 device word that receives this call's SPD_DEVERR_* flags.
  *   The first call on each device looks up the array's device address; make that first
  *   call before capturing any stream.  Every call clears the scratch counters it needs,

@@ -9,27 +9,41 @@
 // :456-466 compute the same quantity over a contiguous or bucketed copy of the cache.
 //
 // B200 design (HBM-bound; no tensor cores):
-// * Work units are pool blocks.  A unit covers one block of ALL heads, which in the
-//   pool layout [num_blocks][block_size][H][D] is one contiguous run of
-//   block_size*H*D elements, fetched with two 1-D bulk async copies (K and V; only the
-//   valid rows of a sequence's last block).
-// * Units of all sequences are laid end to end and every CTA of a persistent grid
-//   (num_SMs x resident CTAs) streams an equal contiguous share, so load balance does
-//   not depend on the context-length distribution.
-// * Warp specialisation: one producer warp (lane 0) runs ahead through an S-stage
-//   shared-memory ring (full mbarriers complete on the copies' bytes; empty mbarriers
-//   collect one arrival per compute warp), so compute warps never meet a CTA-wide
-//   barrier per unit.  Compute warp w owns heads [w*HPW, (w+1)*HPW).
+// * A unit is one pool block of ALL heads: in the pool layout
+//   [num_blocks][block_size][H][D] that is one contiguous run of block_size*H*D
+//   elements, fetched with two 1-D bulk async copies (K and V; only the valid rows of a
+//   sequence's last block).  A work item is up to kItemUnits consecutive units of one
+//   sequence.
+// * Items are handed out dynamically: the producer warp of each CTA of a persistent
+//   grid takes the next item from a global atomic counter (prefetching one take ahead),
+//   so CTAs whose data arrives early simply do more items and the kernel ends when the
+//   item queue drains — the DRAM service order cannot leave stragglers.  The counter is
+//   reset by the last CTA to finish taking.
+// * Set-up is one parallel round trip: the context lengths and the whole block table
+//   come in by bulk copy (when they fit), while the first item is taken.
+// * The producer streams units through an S-stage shared-memory ring (full mbarriers
+//   complete on the copies' bytes, empty mbarriers collect one arrival per compute warp);
+//   per-stage metadata says which sequence/block/item a stage holds; a stage with
+//   sequence -1 ends the loop.  q (and, for the fused append, k_new/v_new) ride in the
+//   stage of an item's first (last) unit.
+// * Compute warp w owns heads [w*HPW, (w+1)*HPW) end to end and never synchronises with
+//   the other compute warps: it patches its own slice of an appended row, and finishes
+//   each (item, head) itself — a whole sequence writes the output; a split one writes a
+//   partial (m, l, acc) to slot [item][h], fences, bumps the (sequence, head) arrival
+//   counter, and the last arrival combines the sequence's partials and resets the counter.
 // * q·k: 32/block_size lanes per row, q (pre-scaled by scale*log2 e) in registers, K
 //   chunks read in a per-row rotated order so the 8 lanes of a shared-memory phase hit
-//   distinct banks.  p·v: each lane owns one 16-byte chunk of a row and the warp walks
-//   32/chunks_per_row rows at a time; partial sums across row groups are folded once per
-//   sequence.  Online softmax in base 2; packed fp32x2 FMAs throughout.
-// * A sequence split across CTAs is merged by the last CTA to finish it: each CTA writes
-//   (m, l, acc) per head to partial slot (b + c); after a CTA barrier one thread fences
-//   and bumps the sequence's arrival counter; the last arrival combines the partials
-//   and resets the counter (no spinning, no second launch).
+//   distinct banks.  p·v: each lane owns one 16-byte chunk of a row.  Online softmax in
+//   base 2; packed fp32x2 FMAs.
+// * Every wait is bounded; a warp whose wait runs out records SPD_DEVERR_TIMEOUT, raises
+//   the CTA's abort flag and leaves, and the others' bounded waits then run out too.
 #include "spd_params.cuh"
+
+// Timeline hook: expands to nothing unless a tracing build defines it (to record
+// %globaltimer at marked points of each CTA).
+#ifndef SPD_TRACE
+#define SPD_TRACE(point) ((void)0)
+#endif
 
 namespace spd {
 
@@ -78,10 +92,6 @@ __device__ __forceinline__ void load_f2(const T* p, float2* out) {
   }
 }
 
-__device__ __forceinline__ void named_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
@@ -102,8 +112,14 @@ struct PagedGeom {
   static_assert((NCH & (NCH - 1)) == 0 && DPL % 2 == 0, "chunking");
 };
 
-constexpr int kPagedComputeBarrier = 1;  // named barrier among compute warps
-constexpr int kIdsWindow = 256;          // block ids preloaded per CTA
+// Per-stage metadata written by the producer before it arms the stage.
+struct StageMeta {
+  int b;      // sequence, or -1: no more work
+  int j;      // block index within the sequence
+  int item;   // global item index
+  int flags;  // kFirst | kLast
+};
+constexpr int kFirst = 1, kLast = 2;
 
 template <typename T, int D, int BS, int HPW>
 __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParams p) {
@@ -112,164 +128,181 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
   constexpr int VE = Gm::VE, CPR = Gm::CPR, RG = Gm::RG, PVP = Gm::PVP;
 
   extern __shared__ __align__(128) unsigned char smem[];
-  const int H = p.H, B = p.B, S = p.stages;
+  const int H = p.H, B = p.B, S = p.stages, MB = p.max_blocks;
   const int HD = H * D;
   const int NW = (H + HPW - 1) / HPW;  // compute warps; warp NW is the producer
-  const int NCT = NW * 32;             // compute threads
   const size_t unit_elems = (size_t)BS * HD;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-  // Stage s: K block, V block, then q / k_new / v_new rows of the unit's sequence.
-  const size_t stage_elems = 2 * unit_elems + 3 * (size_t)HD;
+  // ---- shared memory: ring | barriers | metadata | lengths | item prefix | table ----
+  const size_t stage_elems = 2 * unit_elems + 3 * (size_t)HD;  // K, V, q, k_new, v_new
   T* ring = reinterpret_cast<T*>(smem);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + round_up((size_t)S * stage_elems * sizeof(T), 128));
   uint64_t* empty = full + S;
-  int* prefix = reinterpret_cast<int*>(empty + S);  // [B + 1] unit prefix over sequences
-  int* ctx_s = prefix + B + 1;                      // [B] clamped context lengths
-  int* flag = ctx_s + B;                            // [0] last-arrival, [1] abort
-  int* ids = flag + 2;                              // [kIdsWindow] block ids of this CTA's units
+  uint64_t* setup = empty + S;
+  StageMeta* meta = reinterpret_cast<StageMeta*>(setup + 2);  // 16-byte aligned
+  int* flag = reinterpret_cast<int*>(meta + S);               // [0] abort, [1..3] spare
+  int* ctx_s = flag + 4;                                      // [round4(B)] context lengths
+  int* ip = ctx_s + ((B + 3) & ~3);                           // [B + 1] item prefix
+  int* tab_s = ip + ((B + 4) & ~3);                           // [B * MB] block table copy
+  const bool tab_in_smem = p.table_in_smem != 0;
 
+  int* next_item = p.work + 0;  // global item counter
+  int* done_ctas = p.work + 1;  // CTAs that finished taking items
   const T* __restrict__ kpool = reinterpret_cast<const T*>(p.k_pool);
   const T* __restrict__ vpool = reinterpret_cast<const T*>(p.v_pool);
   T* __restrict__ out = reinterpret_cast<T*>(p.out);
   const T* __restrict__ qg = reinterpret_cast<const T*>(p.q);
   const bool append = p.k_new != nullptr;
-  const int max_ctx = p.max_blocks * BS;
+  const int max_ctx = MB * BS;
 
-  // ---- 1. unit prefix over sequences (every CTA computes it; B is small) ----------
-  for (int i = tid; i < B; i += blockDim.x) {
-    int c = p.context_lens[i];
-    if (c > max_ctx) {
-      set_error(p.err, SPD_DEVERR_LENGTH);
-      c = max_ctx;
-    }
-    c = c > 0 ? c : 0;
-    ctx_s[i] = c;
-    prefix[i + 1] = (c + BS - 1) / BS;
-  }
-  if (tid == 0) {
-    prefix[0] = 0;
-    flag[1] = 0;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    int carry = 0;
-    for (int base = 0; base < B; base += 32) {
-      const int i = base + lane;
-      int v = (i < B) ? prefix[i + 1] : 0;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += n;
-      }
-      if (i < B) prefix[i + 1] = v + carry;
-      carry += __shfl_sync(0xffffffffu, v, 31);
-    }
-  }
-  __syncthreads();
-
-  const long long W = prefix[B];
-  // Effective grid: never more CTAs than units, so every participating CTA owns at
-  // least one unit and the CTAs sharing a sequence are consecutive (which the arrival
-  // count nparts = c_last - c_first + 1 relies on).
-  const int c = blockIdx.x;
-  const int G = (int)((long long)gridDim.x < W ? (long long)gridDim.x : W);
-
-  // ---- 2. sequences with nothing to attend to get zeros (CTA b % gridDim) ----------
-  for (int b = c; b < B; b += gridDim.x) {
-    if (prefix[b + 1] == prefix[b]) {
-      for (int i = tid; i < HD; i += blockDim.x) out[(size_t)b * HD + i] = Elem<T>::from_f(0.f);
-    }
-  }
-  if (W == 0 || c >= G) return;
-  const long long start = range_start(c, G, W), end = range_start(c + 1, G, W);
-
+  if (tid == 0) SPD_TRACE(0);
+  // ---- 1. set-up: barriers, bulk copies of lengths and table, first item take ------
+  const bool ctx_bulk = ((B * 4) % 16 == 0) && ((reinterpret_cast<uintptr_t>(p.context_lens) & 15) == 0);
+  int first_item = 0;
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NW);
     }
+    mbar_init(setup, 1);
     fence_barrier_init();
-  }
-  // Block ids of the first kIdsWindow units of this CTA, loaded in parallel (one round
-  // trip) so the producer never waits on a block-table load.
-  {
-    const long long nids = min(end - start, (long long)kIdsWindow);
-    for (long long i = tid; i < nids; i += blockDim.x) {
-      const long long u = start + i;
-      const int bb = upper_index_i32(prefix, B, u);
-      int phys = p.block_tables[(size_t)bb * p.max_blocks + (u - prefix[bb])];
-      if (phys < 0 || phys >= p.num_blocks) {
-        set_error(p.err, SPD_DEVERR_BLOCK_ID);
-        phys = 0;
-      }
-      ids[i] = phys;
+    const uint32_t tx = (ctx_bulk ? (uint32_t)B * 4u : 0u) + (tab_in_smem ? (uint32_t)B * MB * 4u : 0u);
+    if (tx) {
+      mbar_arrive_expect_tx(setup, tx);
+      if (ctx_bulk) bulk_copy_g2s(ctx_s, p.context_lens, (uint32_t)B * 4u, setup);
+      if (tab_in_smem) bulk_copy_g2s(tab_s, p.block_tables, (uint32_t)B * MB * 4u, setup);
+    } else {
+      mbar_arrive(setup);
     }
   }
+  if (warp == NW && lane == 0) first_item = atomicAdd(next_item, 1);  // overlaps the copies
   __syncthreads();
+  if (!mbar_wait_bounded(setup, 0, p.err)) flag[0] = 1;
+  if (!ctx_bulk) {
+    for (int i = tid; i < B; i += blockDim.x) ctx_s[i] = p.context_lens[i];
+  }
+  __syncthreads();
+  // clamp lengths, items per sequence, and their prefix (warp 0 scans)
+  if (warp == 0) {
+    int carry = 0;
+    for (int base = 0; base < B; base += 32) {
+      const int i = base + lane;
+      int v = 0;
+      if (i < B) {
+        int c = ctx_s[i];
+        if (c > max_ctx) {
+          set_error(p.err, SPD_DEVERR_LENGTH);
+          c = max_ctx;
+        }
+        c = c > 0 ? c : 0;
+        ctx_s[i] = c;
+        const int nblk = (c + BS - 1) / BS;
+        v = (nblk + kItemUnits - 1) / kItemUnits;
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+      }
+      if (i < B) ip[i + 1] = v + carry;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) ip[0] = 0;
+  }
+  __syncthreads();
+  if (tid == 0) SPD_TRACE(1);
+  const int n_items = ip[B];
 
-  // ---- 3. producer warp -------------------------------------------------------------
+  // sequences with nothing to attend to get zeros (CTA b % gridDim, compute threads)
+  for (int b = blockIdx.x; b < B; b += gridDim.x) {
+    if (ctx_s[b] == 0) {
+      for (int i = tid; i < HD; i += blockDim.x) out[(size_t)b * HD + i] = Elem<T>::from_f(0.f);
+    }
+  }
+
+  // ---- 2. producer warp --------------------------------------------------------------
   if (warp == NW) {
     if (lane == 0) {
-      int pb = upper_index_i32(prefix, B, start);
       int s = 0;
       uint32_t ph = 0;
-      long long issued = start;
-      for (long long u = start; u < end; ++u) {
-        if (u - start >= S) {
-          if (*((volatile int*)&flag[1]) || !mbar_wait_bounded(&empty[s], ph ^ 1, p.err)) {
-            flag[1] = 1;
+      long long n_issued = 0;
+      bool alive = !flag[0];
+      int item = first_item;
+      while (alive && item < n_items) {
+        const int nxt = atomicAdd(next_item, 1);  // next take, in flight while this item issues
+        const int b = upper_index_i32(ip, B, item);
+        const int nblk = (ctx_s[b] + BS - 1) / BS;
+        const int j0 = (item - ip[b]) * kItemUnits;
+        const int j1 = min(j0 + kItemUnits, nblk);
+        for (int j = j0; j < j1; ++j) {
+          if (n_issued >= S && (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&empty[s], ph ^ 1, p.err))) {
+            flag[0] = 1;
+            alive = false;
             break;
           }
-        }
-        while (prefix[pb + 1] <= u) ++pb;
-        const int j = (int)(u - prefix[pb]);
-        const int nvalid = min(BS, ctx_s[pb] - j * BS);
-        int phys;
-        if (u - start < kIdsWindow) {
-          phys = ids[u - start];
-        } else {
-          phys = p.block_tables[(size_t)pb * p.max_blocks + j];
+          const int nvalid = min(BS, ctx_s[b] - j * BS);
+          int phys = tab_in_smem ? tab_s[b * MB + j] : p.block_tables[(size_t)b * MB + j];
           if (phys < 0 || phys >= p.num_blocks) {
             set_error(p.err, SPD_DEVERR_BLOCK_ID);
             phys = 0;
           }
+          const bool first = (j == j0), last = (j == j1 - 1);
+          const bool app = append && (j == nblk - 1);
+          meta[s] = StageMeta{b, j, item, (first ? kFirst : 0) | (last ? kLast : 0)};
+          const size_t off = (size_t)phys * unit_elems;
+          const uint32_t bytes = (uint32_t)(nvalid * HD * (int)sizeof(T));
+          const uint32_t row_bytes = (uint32_t)(HD * (int)sizeof(T));
+          T* dst = ring + (size_t)s * stage_elems;
+          mbar_arrive_expect_tx(&full[s], 2 * bytes + (first ? row_bytes : 0u) + (app ? 2 * row_bytes : 0u));
+          bulk_copy_g2s(dst, kpool + off, bytes, &full[s]);
+          bulk_copy_g2s(dst + unit_elems, vpool + off, bytes, &full[s]);
+          if (first) bulk_copy_g2s(dst + 2 * unit_elems, qg + (size_t)b * HD, row_bytes, &full[s]);
+          if (app) {
+            bulk_copy_g2s(dst + 2 * unit_elems + HD, reinterpret_cast<const T*>(p.k_new) + (size_t)b * HD,
+                          row_bytes, &full[s]);
+            bulk_copy_g2s(dst + 2 * unit_elems + 2 * HD, reinterpret_cast<const T*>(p.v_new) + (size_t)b * HD,
+                          row_bytes, &full[s]);
+          }
+          if (n_issued == 0) SPD_TRACE(2);
+          ++n_issued;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
         }
-        const size_t off = (size_t)phys * unit_elems;
-        const uint32_t bytes = (uint32_t)(nvalid * HD * (int)sizeof(T));
-        const uint32_t row_bytes = (uint32_t)(HD * (int)sizeof(T));
-        const bool seg_first = (u == start) || (u == prefix[pb]);
-        const bool app = append && (j == prefix[pb + 1] - prefix[pb] - 1);
-        T* dst = ring + (size_t)s * stage_elems;
-        mbar_arrive_expect_tx(&full[s], 2 * bytes + (seg_first ? row_bytes : 0u) + (app ? 2 * row_bytes : 0u));
-        bulk_copy_g2s(dst, kpool + off, bytes, &full[s]);
-        bulk_copy_g2s(dst + unit_elems, vpool + off, bytes, &full[s]);
-        if (seg_first) bulk_copy_g2s(dst + 2 * unit_elems, qg + (size_t)pb * HD, row_bytes, &full[s]);
-        if (app) {
-          bulk_copy_g2s(dst + 2 * unit_elems + HD, reinterpret_cast<const T*>(p.k_new) + (size_t)pb * HD, row_bytes,
-                        &full[s]);
-          bulk_copy_g2s(dst + 2 * unit_elems + 2 * HD, reinterpret_cast<const T*>(p.v_new) + (size_t)pb * HD,
-                        row_bytes, &full[s]);
-        }
-        issued = u + 1;
-        if (++s == S) {
-          s = 0;
-          ph ^= 1;
-        }
+        item = nxt;
       }
-      // Copies still in flight land before this CTA's shared memory is released:
-      // wait (bounded) for the last phase of every stage that was used.
-      const long long n = issued - start;
-      for (int k = 0; k < S && k < n; ++k) {
-        const long long u = issued - 1 - k;
-        const int st = (int)((u - start) % S);
-        (void)mbar_wait_bounded(&full[st], (uint32_t)(((u - start) / S) & 1), nullptr);
+      SPD_TRACE(3);
+      // end-of-work stage for the compute warps
+      if (alive && n_issued >= S && !mbar_wait_bounded(&empty[s], ph ^ 1, p.err)) alive = false;
+      if (alive) {
+        meta[s] = StageMeta{-1, 0, 0, 0};
+        mbar_arrive(&full[s]);
+      } else {
+        flag[0] = 1;
+      }
+      // This CTA takes no more items; the last CTA to get here re-arms the counter for
+      // the next launch (every CTA's final take has already happened).
+      __threadfence();
+      if (atomicAdd(done_ctas, 1) == (int)gridDim.x - 1) {
+        *((volatile int*)next_item) = 0;
+        *((volatile int*)done_ctas) = 0;
+        __threadfence();
+      }
+      // After an abort, copies still in flight land before this CTA's shared memory is
+      // released (without an abort the compute warps consumed every one of them).
+      if (!alive) {
+        for (int k = 0; k < S && k < n_issued; ++k) {
+          const long long u = n_issued - 1 - k;
+          (void)mbar_wait_bounded(&full[u % S], (uint32_t)((u / S) & 1), nullptr);
+        }
       }
     }
     return;
   }
 
-  // ---- 4. compute warps -----------------------------------------------------------------
+  // ---- 3. compute warps (independent of each other) ----------------------------------
   const int r = lane / LPR;    // q·k row of this lane
   const int sub = lane % LPR;  // which DPL-slice of the row
   const int rot = r & (NCH - 1);
@@ -279,23 +312,28 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
   float2 qr[HPW][DPL / 2];
   float m[HPW], l[HPW];
   float2 acc[HPW][VE / 2];
-
-  int b = upper_index_i32(prefix, B, start);
-  bool need_q = true;
   int s = 0;
   uint32_t ph = 0;
+  bool traced = false;
 
-  for (long long g = start; g < end; ++g) {
-    const bool ok = !*((volatile int*)&flag[1]) && mbar_wait_bounded(&full[s], ph, p.err);
-    if (!ok) flag[1] = 1;
-    const int j = (int)(g - prefix[b]);
-    const int nblk = prefix[b + 1] - prefix[b];
+  for (;;) {
+    if (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&full[s], ph, p.err)) {
+      flag[0] = 1;
+      return;
+    }
+    const StageMeta mt = meta[s];
+    if (mt.b < 0) break;
+    if (tid == 0 && !traced) {
+      SPD_TRACE(4);
+      traced = true;
+    }
+    const int b = mt.b, j = mt.j;
     const int nvalid = min(BS, ctx_s[b] - j * BS);
     T* Ks = ring + (size_t)s * stage_elems;
     T* Vs = Ks + unit_elems;
-    const T* Qs = Vs + unit_elems;  // q row of sequence b (first unit of a segment only)
+    const T* Qs = Vs + unit_elems;
 
-    if (need_q) {
+    if (mt.flags & kFirst) {
 #pragma unroll
       for (int k = 0; k < HPW; ++k) {
         const int h = warp * HPW + k;
@@ -303,7 +341,7 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
         l[k] = 0.f;
 #pragma unroll
         for (int i = 0; i < VE / 2; ++i) acc[k][i] = make_float2(0.f, 0.f);
-        if (h < H && ok) {
+        if (h < H) {
           const T* qrow = Qs + h * D + sub * DPL;
 #pragma unroll
           for (int cc = 0; cc < NCH; ++cc) {
@@ -317,82 +355,77 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
           }
         }
       }
-      need_q = false;
     }
 
+    const int nblk = (ctx_s[b] + BS - 1) / BS;
     if (append && j == nblk - 1) {
-      // op (3) fused: the new token sits at row nvalid-1 of the sequence's last block.
-      int phys = p.block_tables[(size_t)b * p.max_blocks + j];
+      // op (3) fused: the new token is row nvalid-1 of the last block; this warp writes
+      // its own heads' slice into the stage (so its q·k sees it) and into the pool.
+      int phys = tab_in_smem ? tab_s[b * MB + j] : p.block_tables[(size_t)b * MB + j];
       if (phys < 0 || phys >= p.num_blocks) phys = 0;  // flagged by the producer
       const size_t row_off = (size_t)(nvalid - 1) * HD;
-      T* kdst = const_cast<T*>(kpool) + (size_t)phys * unit_elems + row_off;
-      T* vdst = const_cast<T*>(vpool) + (size_t)phys * unit_elems + row_off;
-      const T* ksrc = Qs + HD;  // k_new / v_new rows arrived with this unit
-      const T* vsrc = Qs + 2 * HD;
       constexpr int VEC = 16 / sizeof(T);
-      if (ok) {
-        for (int i = tid * VEC; i < HD; i += NCT * VEC) {
-          const uint4 kv = *reinterpret_cast<const uint4*>(ksrc + i);
-          const uint4 vv = *reinterpret_cast<const uint4*>(vsrc + i);
-          *reinterpret_cast<uint4*>(Ks + row_off + i) = kv;
-          *reinterpret_cast<uint4*>(Vs + row_off + i) = vv;
-          *reinterpret_cast<uint4*>(kdst + i) = kv;
-          *reinterpret_cast<uint4*>(vdst + i) = vv;
+      for (int k = 0; k < HPW; ++k) {
+        const int h = warp * HPW + k;
+        if (h >= H) break;
+        for (int i = lane * VEC; i < D; i += 32 * VEC) {
+          const size_t e = row_off + (size_t)h * D + i;
+          const uint4 kv = *reinterpret_cast<const uint4*>(Qs + HD + h * D + i);
+          const uint4 vv = *reinterpret_cast<const uint4*>(Qs + 2 * HD + h * D + i);
+          *reinterpret_cast<uint4*>(Ks + e) = kv;
+          *reinterpret_cast<uint4*>(Vs + e) = vv;
+          *reinterpret_cast<uint4*>(const_cast<T*>(kpool) + (size_t)phys * unit_elems + e) = kv;
+          *reinterpret_cast<uint4*>(const_cast<T*>(vpool) + (size_t)phys * unit_elems + e) = vv;
         }
       }
       fence_proxy_async_smem();  // generic writes before the next bulk copy into this stage
-      named_sync(kPagedComputeBarrier, NCT);
+      __syncwarp();
     }
 
-    if (ok) {
 #pragma unroll
-      for (int k = 0; k < HPW; ++k) {
-        const int h = warp * HPW + k;
-        if (h >= H) continue;
-        const T* Kh = Ks + h * D;
-        const T* Vh = Vs + h * D;
-        // q·k for row r
-        float sc = -INFINITY;
-        if (r < nvalid) {
-          const T* krow = Kh + (size_t)r * HD + sub * DPL;
-          float2 dot = make_float2(0.f, 0.f);
+    for (int k = 0; k < HPW; ++k) {
+      const int h = warp * HPW + k;
+      if (h >= H) continue;
+      const T* Kh = Ks + h * D;
+      const T* Vh = Vs + h * D;
+      float sc = -INFINITY;
+      if (r < nvalid) {
+        const T* krow = Kh + (size_t)r * HD + sub * DPL;
+        float2 dot = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int cc = 0; cc < NCH; ++cc) {
-            const int ci = (cc + rot) & (NCH - 1);
-            float2 kv[CH / 2];
-            load_f2<T, CH>(krow + ci * CH, kv);
+        for (int cc = 0; cc < NCH; ++cc) {
+          const int ci = (cc + rot) & (NCH - 1);
+          float2 kv[CH / 2];
+          load_f2<T, CH>(krow + ci * CH, kv);
 #pragma unroll
-            for (int e = 0; e < CH / 2; ++e) dot = __ffma2_rn(qr[k][cc * CH / 2 + e], kv[e], dot);
-          }
-          sc = dot.x + dot.y;
+          for (int e = 0; e < CH / 2; ++e) dot = __ffma2_rn(qr[k][cc * CH / 2 + e], kv[e], dot);
         }
+        sc = dot.x + dot.y;
+      }
 #pragma unroll
-        for (int o = 1; o < LPR; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
-        if (r >= nvalid) sc = -INFINITY;
-        const float mnew = fmaxf(m[k], warp_max(sc));
-        const float alpha = exp2f(m[k] - mnew);
-        const float pr = (r < nvalid) ? exp2f(sc - mnew) : 0.f;
-        l[k] = l[k] * alpha + (sub == 0 ? pr : 0.f);
-        m[k] = mnew;
-        const float2 a2 = make_float2(alpha, alpha);
+      for (int o = 1; o < LPR; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+      if (r >= nvalid) sc = -INFINITY;
+      const float mnew = fmaxf(m[k], warp_max(sc));
+      const float alpha = exp2f(m[k] - mnew);
+      const float pr = (r < nvalid) ? exp2f(sc - mnew) : 0.f;
+      l[k] = l[k] * alpha + (sub == 0 ? pr : 0.f);
+      m[k] = mnew;
+      const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
-        for (int i = 0; i < VE / 2; ++i) acc[k][i] = __fmul2_rn(acc[k][i], a2);
-        // p·v: this lane's 16-byte chunk of rows rg, rg+RG, ...
+      for (int i = 0; i < VE / 2; ++i) acc[k][i] = __fmul2_rn(acc[k][i], a2);
 #pragma unroll
-        for (int ps = 0; ps < PVP; ++ps) {
-          const int rr = ps * RG + rg;
-          const float prr = __shfl_sync(0xffffffffu, pr, (rr < BS ? rr : 0) * LPR);
-          if (rr < nvalid) {
-            float2 vv[VE / 2];
-            load_f2<T, VE>(Vh + (size_t)rr * HD + cidx * VE, vv);
-            const float2 p2 = make_float2(prr, prr);
+      for (int ps = 0; ps < PVP; ++ps) {
+        const int rr = ps * RG + rg;
+        const float prr = __shfl_sync(0xffffffffu, pr, (rr < BS ? rr : 0) * LPR);
+        if (rr < nvalid) {
+          float2 vv[VE / 2];
+          load_f2<T, VE>(Vh + (size_t)rr * HD + cidx * VE, vv);
+          const float2 p2 = make_float2(prr, prr);
 #pragma unroll
-            for (int i = 0; i < VE / 2; ++i) acc[k][i] = __ffma2_rn(p2, vv[i], acc[k][i]);
-          }
+          for (int i = 0; i < VE / 2; ++i) acc[k][i] = __ffma2_rn(p2, vv[i], acc[k][i]);
         }
       }
     }
-    // this warp is done with stage s
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     if (++s == S) {
@@ -400,107 +433,83 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
       ph ^= 1;
     }
 
-    // ---- segment end: finish sequence b -------------------------------------------
-    const bool seq_end = (g + 1 == prefix[b + 1]);
-    if (seq_end || g + 1 == end) {
-      const bool whole = (start <= prefix[b]) && (end >= prefix[b + 1]);
-      float ltot[HPW];
+    if (!(mt.flags & kLast)) continue;
+    // ---- item end: this warp finishes its heads for (item, b) ---------------------------
+    const int i0 = ip[b], nitems = ip[b + 1] - ip[b];
 #pragma unroll
-      for (int k = 0; k < HPW; ++k) {
-        ltot[k] = warp_sum(l[k]);
+    for (int k = 0; k < HPW; ++k) {
+      const int h = warp * HPW + k;
+      if (h >= H) continue;
+      const float ltot = warp_sum(l[k]);
 #pragma unroll
-        for (int o = CPR; o < 32; o <<= 1)
+      for (int o = CPR; o < 32; o <<= 1)
+#pragma unroll
+        for (int i = 0; i < VE / 2; ++i) {
+          acc[k][i].x += __shfl_xor_sync(0xffffffffu, acc[k][i].x, o);
+          acc[k][i].y += __shfl_xor_sync(0xffffffffu, acc[k][i].y, o);
+        }
+      T* orow = out + ((size_t)b * H + h) * D + cidx * VE;
+      if (nitems == 1) {
+        if (rg == 0) {
+          const float inv = 1.f / ltot;
 #pragma unroll
           for (int i = 0; i < VE / 2; ++i) {
-            acc[k][i].x += __shfl_xor_sync(0xffffffffu, acc[k][i].x, o);
-            acc[k][i].y += __shfl_xor_sync(0xffffffffu, acc[k][i].y, o);
+            orow[2 * i] = Elem<T>::from_f(acc[k][i].x * inv);
+            orow[2 * i + 1] = Elem<T>::from_f(acc[k][i].y * inv);
           }
+        }
+        continue;
       }
-      if (whole) {
+      float* slot = p.partials + ((size_t)mt.item * H + h) * (D + 2);
+      if (rg == 0) {
 #pragma unroll
-        for (int k = 0; k < HPW; ++k) {
-          const int h = warp * HPW + k;
-          if (h < H && rg == 0) {
-            const float inv = 1.f / ltot[k];
-            T* o = out + ((size_t)b * H + h) * D + cidx * VE;
-#pragma unroll
-            for (int i = 0; i < VE / 2; ++i) {
-              o[2 * i] = Elem<T>::from_f(acc[k][i].x * inv);
-              o[2 * i + 1] = Elem<T>::from_f(acc[k][i].y * inv);
-            }
-          }
-        }
-      } else {
-        const long long p0 = prefix[b], p1 = prefix[b + 1];
-        const int c_first = cta_of_unit(p0, G, W);
-        const int c_last = cta_of_unit(p1 - 1, G, W);
-        const int nparts = c_last - c_first + 1;
-#pragma unroll
-        for (int k = 0; k < HPW; ++k) {
-          const int h = warp * HPW + k;
-          if (h < H) {
-            float* slot = p.partials + ((size_t)(b + c) * H + h) * (D + 2);
-            if (rg == 0) {
-#pragma unroll
-              for (int i = 0; i < VE / 2; ++i)
-                *reinterpret_cast<float2*>(slot + cidx * VE + 2 * i) = acc[k][i];
-            }
-            if (lane == 0) {
-              slot[D] = m[k];
-              slot[D + 1] = ltot[k];
-            }
-          }
-        }
-        // every compute thread's partial writes precede thread 0's fence + arrival
-        named_sync(kPagedComputeBarrier, NCT);
-        if (tid == 0) {
+        for (int i = 0; i < VE / 2; ++i) *reinterpret_cast<float2*>(slot + cidx * VE + 2 * i) = acc[k][i];
+      }
+      if (lane == 0) {
+        slot[D] = m[k];
+        slot[D + 1] = ltot;
+      }
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        __threadfence();
+        int* cnt = p.counters + (size_t)b * H + h;
+        last = (atomicAdd(cnt, 1) == nitems - 1);
+        if (last) {
+          *cnt = 0;  // every item of (b, h) has arrived; ready for the next call
           __threadfence();
-          const int old = atomicAdd(&p.counters[b], 1);
-          const int last = (old == nparts - 1);
-          if (last) {
-            p.counters[b] = 0;  // every part has arrived; ready for the next call
-            __threadfence();
-          }
-          flag[0] = last;
-        }
-        named_sync(kPagedComputeBarrier, NCT);
-        if (flag[0]) {
-          for (int h = warp; h < H; h += NW) {
-            float M = -INFINITY;
-            for (int cc = c_first; cc <= c_last; ++cc)
-              M = fmaxf(M, __ldcg(p.partials + ((size_t)(b + cc) * H + h) * (D + 2) + D));
-            float L = 0.f;
-            float2 o[VE / 2];
-#pragma unroll
-            for (int i = 0; i < VE / 2; ++i) o[i] = make_float2(0.f, 0.f);
-            for (int cc = c_first; cc <= c_last; ++cc) {
-              const float* slot = p.partials + ((size_t)(b + cc) * H + h) * (D + 2);
-              const float w = exp2f(__ldcg(slot + D) - M);
-              L = fmaf(__ldcg(slot + D + 1), w, L);
-              const float2 w2 = make_float2(w, w);
-#pragma unroll
-              for (int i = 0; i < VE / 2; ++i)
-                o[i] = __ffma2_rn(__ldcg(reinterpret_cast<const float2*>(slot + cidx * VE + 2 * i)), w2, o[i]);
-            }
-            if (rg == 0) {
-              const float inv = 1.f / L;
-              T* op = out + ((size_t)b * H + h) * D + cidx * VE;
-#pragma unroll
-              for (int i = 0; i < VE / 2; ++i) {
-                op[2 * i] = Elem<T>::from_f(o[i].x * inv);
-                op[2 * i + 1] = Elem<T>::from_f(o[i].y * inv);
-              }
-            }
-          }
         }
       }
-      if (seq_end) {
-        ++b;
-        while (b < B && prefix[b + 1] == prefix[b]) ++b;
-        need_q = true;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      __threadfence();  // every lane reads the other CTAs' partials after the arrival
+      float M = -INFINITY;
+      for (int it = 0; it < nitems; ++it)
+        M = fmaxf(M, __ldcg(p.partials + ((size_t)(i0 + it) * H + h) * (D + 2) + D));
+      float L = 0.f;
+      float2 o[VE / 2];
+#pragma unroll
+      for (int i = 0; i < VE / 2; ++i) o[i] = make_float2(0.f, 0.f);
+      for (int it = 0; it < nitems; ++it) {
+        const float* sl = p.partials + ((size_t)(i0 + it) * H + h) * (D + 2);
+        const float w = exp2f(__ldcg(sl + D) - M);
+        L = fmaf(__ldcg(sl + D + 1), w, L);
+        const float2 w2 = make_float2(w, w);
+#pragma unroll
+        for (int i = 0; i < VE / 2; ++i)
+          o[i] = __ffma2_rn(__ldcg(reinterpret_cast<const float2*>(sl + cidx * VE + 2 * i)), w2, o[i]);
+      }
+      if (rg == 0) {
+        const float inv = 1.f / L;
+#pragma unroll
+        for (int i = 0; i < VE / 2; ++i) {
+          orow[2 * i] = Elem<T>::from_f(o[i].x * inv);
+          orow[2 * i + 1] = Elem<T>::from_f(o[i].y * inv);
+        }
       }
     }
   }
+  if (tid == 0) SPD_TRACE(5);
 }
 
 // ------------------------------------------------------------------ host launcher
@@ -510,15 +519,22 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
   const int nw = (p.H + HPW - 1) / HPW;
   const int threads = (nw + 1) * 32;
   const size_t stage_bytes = ((size_t)2 * BS + 3) * p.H * D * sizeof(T);
-  // Ring depth: up to ~216 KB of stages per CTA (one CTA per SM at the Whisper shapes;
-  // the producer warp keeps every stage in flight), at least two stages.
-  const size_t fixed = 16 * 8 + 4 * (2 * (size_t)p.B + 3 + kIdsWindow) + 256;
-  int S = (int)((216 * 1024 - fixed) / stage_bytes);
+  const size_t tab_bytes = (size_t)p.B * p.max_blocks * 4;
+  p.table_in_smem = (tab_bytes <= kTableSmemMax && tab_bytes % 16 == 0 &&
+                     (reinterpret_cast<uintptr_t>(p.block_tables) & 15) == 0)
+                        ? 1
+                        : 0;
+  const size_t fixed = 16 * 8 /*barriers*/ + 16 * 8 /*meta*/ + 16 + 4 * ((size_t)p.B + 4) * 2 +
+                       (p.table_in_smem ? tab_bytes : 0) + 256;
+  // Ring depth: up to ~216 KB per CTA (one CTA per SM at the Whisper shapes; the
+  // producer warp keeps every stage in flight), at least two stages.
+  int S = (int)((216 * 1024 > fixed ? 216 * 1024 - fixed : 0) / stage_bytes);
   if (S < 2 && 2 * stage_bytes + fixed <= 227 * 1024) S = 2;
   S = S < 1 ? 1 : (S > 8 ? 8 : S);
   p.stages = S;
-  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * (size_t)S +
-                      4 * (2 * (size_t)p.B + 3 + kIdsWindow);
+  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * ((size_t)S * 2 + 2) + 16 * (size_t)S + 16 +
+                      4 * ((((size_t)p.B + 3) & ~(size_t)3) + (((size_t)p.B + 4) & ~(size_t)3)) +
+                      (p.table_in_smem ? tab_bytes : 0);
   if (smem > 227 * 1024) return SPD_ERR_UNSUPPORTED;
   auto kfn = paged_decode_attn_kernel<T, D, BS, HPW>;
   if (smem > 48 * 1024 &&

@@ -52,25 +52,26 @@ extern "C" int spd_paged_decode_attn_noalloc(const void* q, void* k_pool, void* 
                                              void* out, int B, int H, int D, int block_size, int max_blocks,
                                              int num_blocks, float scale, int dtype, const void* k_new,
                                              const void* v_new, int32_t* error_word, void* stream) {
-  if (B <= 0 || H <= 0 || D <= 0)
-    return spd::record_error(SPD_ERR_INVALID_ARG, "spd_paged_decode_attn_noalloc: B, H and D must be positive");
-  const size_t need = spd_paged_decode_attn_workspace_size(B, H, D, -1);
+  if (B <= 0 || H <= 0 || D <= 0 || max_blocks <= 0)
+    return spd::record_error(SPD_ERR_INVALID_ARG,
+                             "spd_paged_decode_attn_noalloc: B, H, D and max_blocks must be positive");
+  const size_t need = spd_paged_decode_attn_workspace_size(B, H, D, max_blocks, -1);
   if (need == 0) return spd::record_error(SPD_ERR_CUDA, "spd_paged_decode_attn_noalloc: no CUDA device");
   if (need > SPD_NOALLOC_SCRATCH_BYTES) {
     char msg[256];
     snprintf(msg, sizeof(msg),
-             "spd_paged_decode_attn_noalloc: B=%d H=%d D=%d needs %zu bytes of scratch, more than the %u-byte "
-             "array; use spd_paged_decode_attn with a workspace",
-             B, H, D, need, (unsigned)SPD_NOALLOC_SCRATCH_BYTES);
+             "spd_paged_decode_attn_noalloc: B=%d H=%d D=%d max_blocks=%d needs %zu bytes of scratch, more "
+             "than the %u-byte array; use spd_paged_decode_attn with a workspace",
+             B, H, D, max_blocks, need, (unsigned)SPD_NOALLOC_SCRATCH_BYTES);
     return spd::record_error(SPD_ERR_WORKSPACE, msg);
   }
   void* scratch = nullptr;
   int rc = scratch_for_current_device(&scratch);
   if (rc != SPD_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The header (error word) and the arrival counters must start at zero; the previous
-  // call may have used another batch size, which moves where the counters sit.
-  const size_t clear = spd::kWsHeaderBytes + spd::round_up((size_t)B * 4, 256);
+  // The header (error word, work counters) and the arrival counters must start at zero;
+  // the previous call may have used another geometry, which moves where they sit.
+  const size_t clear = spd::kWsHeaderBytes + spd::round_up((size_t)B * H * 4, 256);
   if (cudaMemsetAsync(scratch, 0, clear, st) != cudaSuccess)
     return spd::record_error(SPD_ERR_CUDA, "spd_paged_decode_attn_noalloc: clearing the scratch counters failed");
   rc = spd_paged_decode_attn(q, k_pool, v_pool, block_tables, context_lens, out, B, H, D, block_size, max_blocks,

@@ -91,12 +91,11 @@ int spd_get_last_error(char* buf, size_t size) {
   return g_err_code;
 }
 
-size_t spd_paged_decode_attn_workspace_size(int B, int H, int D, int device) {
-  const int sms = sm_count(device);
-  if (B <= 0 || H <= 0 || D <= 0 || sms <= 0) return 0;
-  const size_t grid = (size_t)sms * spd::kMaxCtasPerSm;
-  return spd::kWsHeaderBytes + spd::round_up((size_t)B * 4, 256) +
-         spd::round_up(((size_t)B + grid) * H * (D + 2) * 4, 256);
+size_t spd_paged_decode_attn_workspace_size(int B, int H, int D, int max_blocks, int device) {
+  if (B <= 0 || H <= 0 || D <= 0 || max_blocks <= 0 || sm_count(device) <= 0) return 0;
+  const size_t items = (size_t)B * ((max_blocks + spd::kItemUnits - 1) / spd::kItemUnits);
+  return spd::kWsHeaderBytes + spd::round_up((size_t)B * H * 4, 256) +
+         spd::round_up(items * H * (D + 2) * 4, 256);
 }
 
 size_t spd_cross_attn_workspace_size(int B, int H, int D, int device) {
@@ -135,7 +134,7 @@ int spd_paged_decode_attn(const void* q, void* k_pool, void* v_pool, const int32
   if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out) ||
       (k_new && (!aligned16(k_new) || !aligned16(v_new))))
     return fail(SPD_ERR_INVALID_ARG, "spd_paged_decode_attn: tensors must be 16-byte aligned");
-  const size_t need = spd_paged_decode_attn_workspace_size(B, H, D, -1);
+  const size_t need = spd_paged_decode_attn_workspace_size(B, H, D, max_blocks, -1);
   if (!workspace || workspace_bytes < need)
     return fail(SPD_ERR_WORKSPACE, "spd_paged_decode_attn: workspace %zu bytes, need %zu", workspace_bytes, need);
   const int sms = sm_count(-1);
@@ -148,8 +147,9 @@ int spd_paged_decode_attn(const void* q, void* k_pool, void* v_pool, const int32
   p.scale_log2 = scale * 1.4426950408889634f;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   p.err = reinterpret_cast<int*>(ws);
+  p.work = reinterpret_cast<int*>(ws + spd::kWsWorkOffset);
   p.counters = reinterpret_cast<int*>(ws + spd::kWsHeaderBytes);
-  p.partials = reinterpret_cast<float*>(ws + spd::kWsHeaderBytes + spd::round_up((size_t)B * 4, 256));
+  p.partials = reinterpret_cast<float*>(ws + spd::kWsHeaderBytes + spd::round_up((size_t)B * H * 4, 256));
   const int rc = spd::paged_decode_attn_launch(p, dtype, D, block_size, sms, static_cast<cudaStream_t>(stream));
   if (rc == SPD_ERR_UNSUPPORTED)
     return fail(rc, "spd_paged_decode_attn: H=%d D=%d block_size=%d dtype=%d does not fit shared memory", H, D,

@@ -22,6 +22,12 @@ constexpr size_t kWsHeaderBytes = 256;
 // Upper bound on resident CTAs per SM that any attention launch uses; the partial-slot
 // region is sized for grid <= num_SMs * kMaxCtasPerSm.
 constexpr int kMaxCtasPerSm = 4;
+// Paged attention work item: up to this many consecutive pool blocks of one sequence.
+constexpr int kItemUnits = 2;
+// Block tables up to this size are bulk-copied into each CTA's shared memory.
+constexpr size_t kTableSmemMax = 16384;
+// Workspace header: error word at byte 0, the paged kernel's item counters at byte 128.
+constexpr size_t kWsWorkOffset = 128;
 // Bounded wait: 2 s of %globaltimer.
 constexpr unsigned long long SPD_WAIT_NS = 2000000000ull;
 

@@ -18,9 +18,11 @@ struct PagedParams {
   int B, H, max_blocks, num_blocks;
   float scale_log2;  // scale * log2(e)
   int* err;          // workspace error word
-  int* counters;     // [B] arrival counters (left at zero)
-  float* partials;   // [(B + grid) * H * (D + 2)]
+  int* work;         // [0] next item to take, [1] CTAs done taking (both left at zero)
+  int* counters;     // [B * H] arrival counters per (sequence, head) (left at zero)
+  float* partials;   // [B * ceil(max_blocks / kItemUnits) * H * (D + 2)]
   int stages;
+  int table_in_smem;  // the whole block table is bulk-copied into shared memory
 };
 
 struct CrossParams {

@@ -34,7 +34,7 @@ _vp, _i, _i64, _f, _sz = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
 _SIGNATURES = {
     "spd_version": (_i, []),
     "spd_get_last_error": (_i, [C.c_char_p, _sz]),
-    "spd_paged_decode_attn_workspace_size": (_sz, [_i, _i, _i, _i]),
+    "spd_paged_decode_attn_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "spd_cross_attn_workspace_size": (_sz, [_i, _i, _i, _i]),
     "spd_read_error_word": (_i, [_vp, C.POINTER(C.c_int32), _vp]),
     "spd_paged_decode_attn": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i,

@@ -61,11 +61,11 @@ def _stream_handle() -> int:
 _WORKSPACES: Dict[Tuple, torch.Tensor] = {}
 
 
-def paged_attn_workspace(B: int, H: int, D: int, device: torch.device) -> torch.Tensor:
-    """Zero-filled workspace for ``paged_decode_attention`` (reusable on one stream)."""
-    N.load()
+def paged_attn_workspace(B: int, H: int, D: int, max_blocks: int, device: torch.device) -> torch.Tensor:
+    """Zero-filled workspace for ``paged_decode_attention`` over ``B`` sequences with
+    block tables of ``max_blocks`` columns (reusable on one stream)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    n = N.load().spd_paged_decode_attn_workspace_size(B, H, D, idx)
+    n = N.load().spd_paged_decode_attn_workspace_size(B, H, D, max_blocks, idx)
     if n == 0:
         raise RuntimeError("paged_attn_workspace: could not size workspace (no CUDA device?)")
     return torch.zeros(n, dtype=torch.uint8, device=device)
@@ -80,14 +80,15 @@ def cross_attn_workspace(B: int, H: int, D: int, device: torch.device) -> torch.
     return torch.zeros(n, dtype=torch.uint8, device=device)
 
 
-def _cached_workspace(kind: str, B: int, H: int, D: int, device: torch.device) -> torch.Tensor:
+def _cached_workspace(kind: str, B: int, H: int, D: int, device: torch.device, max_blocks: int = 0) -> torch.Tensor:
     """One zero-initialised workspace per (op, geometry, device, stream).  The counter and
     partial regions are laid out by geometry, so a workspace is never shared between
     geometries (stale partials would otherwise land in another call's counters)."""
-    key = (kind, B, H, D, device, torch.cuda.current_stream(device).cuda_stream)
+    key = (kind, B, H, D, max_blocks, device, torch.cuda.current_stream(device).cuda_stream)
     ws = _WORKSPACES.get(key)
     if ws is None:
-        ws = (paged_attn_workspace if kind == "paged" else cross_attn_workspace)(B, H, D, device)
+        ws = (paged_attn_workspace(B, H, D, max_blocks, device) if kind == "paged"
+              else cross_attn_workspace(B, H, D, device))
         _WORKSPACES[key] = ws
     return ws
 
@@ -154,7 +155,7 @@ def paged_decode_attention(
     elif out.shape != (B, H, D) or not out.is_contiguous() or out.dtype != q.dtype:
         raise RuntimeError("paged_decode_attention: out must be a contiguous [B, H, D] tensor of q's dtype")
     if workspace is None:
-        workspace = _cached_workspace("paged", B, H, D, dev)
+        workspace = _cached_workspace("paged", B, H, D, dev, block_tables.shape[1])
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     lib = N.load()

@@ -30,7 +30,7 @@ def _paged(dev, sets):
         kp = torch.randn(NB, bs, H, D, device=dev).half()
         vp = torch.randn(NB, bs, H, D, device=dev).half()
         out.append((q, kp, vp, tables.to(dev), ctx.to(dev)))
-    ws = ops.paged_attn_workspace(B, H, D, dev)
+    ws = ops.paged_attn_workspace(B, H, D, 28, dev)
     return lambda i: ops.paged_decode_attention(*out[i % sets], scale=0.125, workspace=ws)
 
 

@@ -167,12 +167,14 @@ def test_paged_attention_repeat_calls_and_counters_reset():
     ctx = rng.integers(1, 449, B).astype(np.int32)
     nb = int(sum(-(-int(c) // bs) for c in ctx)) + 4
     tq, tk, tv, tt, tc, *_ = _random_paged(rng, B, H, D, bs, nb, ctx, torch.float16)
-    ws = ops.paged_attn_workspace(B, H, D, tq.device)
+    ws = ops.paged_attn_workspace(B, H, D, tt.shape[1], tq.device)
     a = ops.paged_decode_attention(tq, tk, tv, tt, tc, workspace=ws)
     b = ops.paged_decode_attention(tq, tk, tv, tt, tc, workspace=ws)
     assert torch.equal(a, b)
-    counters = ws[256 : 256 + 4 * B].view(torch.int32)
+    counters = ws[256 : 256 + 4 * B * H].view(torch.int32)  # per (sequence, head)
     assert not counters.any()
+    work = ws[128:136].view(torch.int32)  # item counter and done-CTA counter
+    assert not work.any()
     assert ops.read_error_word(ws) == 0
 
 
@@ -182,7 +184,7 @@ def test_paged_attention_poisoned_table_sets_error_word_without_fault():
     ctx = np.array([20, 5, 40, 1], np.int32)
     tq, tk, tv, tt, tc, *_ = _random_paged(rng, B, H, D, bs, 16, ctx, torch.float16)
     tt[2, 1] = 10_000  # block id beyond the pool
-    ws = ops.paged_attn_workspace(B, H, D, tq.device)
+    ws = ops.paged_attn_workspace(B, H, D, tt.shape[1], tq.device)
     ops.paged_decode_attention(tq, tk, tv, tt, tc, workspace=ws)
     assert ops.read_error_word(ws) & N.SPD_DEVERR_BLOCK_ID
     ws.zero_()
@@ -199,7 +201,7 @@ def test_paged_attention_in_cuda_graph():
     ctx = rng.integers(1, 300, B).astype(np.int32)
     nb = int(sum(-(-int(c) // bs) for c in ctx)) + 4
     tq, tk, tv, tt, tc, *_ = _random_paged(rng, B, H, D, bs, nb, ctx, torch.float16)
-    ws = ops.paged_attn_workspace(B, H, D, tq.device)
+    ws = ops.paged_attn_workspace(B, H, D, tt.shape[1], tq.device)
     out = torch.empty_like(tq)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
