@@ -160,6 +160,7 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
   // ---- 1. set-up: barriers, bulk copies of lengths and table, first item take ------
   const bool ctx_bulk = ((B * 4) % 16 == 0) && ((reinterpret_cast<uintptr_t>(p.context_lens) & 15) == 0);
   int first_item = 0;
+  if (tid < 4) flag[tid] = 0;  // shared memory starts undefined
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
