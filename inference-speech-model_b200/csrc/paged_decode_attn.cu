@@ -26,11 +26,14 @@
 //   per-stage metadata says which sequence/block/item a stage holds; a stage with
 //   sequence -1 ends the loop.  q (and, for the fused append, k_new/v_new) ride in the
 //   stage of an item's first (last) unit.
-// * Compute warp w owns heads [w*HPW, (w+1)*HPW) end to end and never synchronises with
-//   the other compute warps: it patches its own slice of an appended row, and finishes
-//   each (item, head) itself — a whole sequence writes the output; a split one writes a
-//   partial (m, l, acc) to slot [item][h], fences, bumps the (sequence, head) arrival
-//   counter, and the last arrival combines the sequence's partials and resets the counter.
+// * Compute warp w owns heads [w*HPW, (w+1)*HPW) and never synchronises with the other
+//   compute warps: it patches its own slice of an appended row; at the end of an item it
+//   writes the output (an item covering the whole sequence) or a partial (m, l, acc) to
+//   slot [item][h] and hands the item to the flush warp through a small mbarrier ring.
+// * The flush warp takes the latency of split-KV merging off the compute warps: per
+//   handed-over item it fences, bumps the sequence's arrival counter, and when it is the
+//   last arrival it combines the sequence's partials for all heads and resets the
+//   counter (no spinning, no second launch).
 // * q·k: 32/block_size lanes per row, q (pre-scaled by scale*log2 e) in registers, K
 //   chunks read in a per-row rotated order so the 8 lanes of a shared-memory phase hit
 //   distinct banks.  p·v: each lane owns one 16-byte chunk of a row.  Online softmax in
@@ -113,6 +116,8 @@ struct PagedGeom {
 };
 
 // Per-stage metadata written by the producer before it arms the stage.
+constexpr int kFlushSlots = 4;  // items in flight between compute warps and the flush warp
+
 struct StageMeta {
   int b;      // sequence, or -1: no more work
   int j;      // block index within the sequence
@@ -122,7 +127,7 @@ struct StageMeta {
 constexpr int kFirst = 1, kLast = 2;
 
 template <typename T, int D, int BS, int HPW>
-__global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParams p) {
+__global__ void __launch_bounds__(576) paged_decode_attn_kernel(const PagedParams p) {
   using Gm = PagedGeom<T, D, BS>;
   constexpr int LPR = Gm::LPR, DPL = Gm::DPL, CH = Gm::CH, NCH = Gm::NCH;
   constexpr int VE = Gm::VE, CPR = Gm::CPR, RG = Gm::RG, PVP = Gm::PVP;
@@ -140,8 +145,11 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + round_up((size_t)S * stage_elems * sizeof(T), 128));
   uint64_t* empty = full + S;
   uint64_t* setup = empty + S;
-  StageMeta* meta = reinterpret_cast<StageMeta*>(setup + 2);  // 16-byte aligned
-  int* flag = reinterpret_cast<int*>(meta + S);               // [0] abort, [1..3] spare
+  uint64_t* fbar = setup + 2;                                 // [kFlushSlots] items handed over
+  uint64_t* fempty = fbar + kFlushSlots;                      // [kFlushSlots] slots free again
+  StageMeta* meta = reinterpret_cast<StageMeta*>(fempty + kFlushSlots);  // 16-byte aligned
+  int4* fmeta = reinterpret_cast<int4*>(meta + S);            // [kFlushSlots] {b, item, nitems, -}
+  int* flag = reinterpret_cast<int*>(fmeta + kFlushSlots);    // [0] abort, [1..3] spare
   int* ctx_s = flag + 4;                                      // [round4(B)] context lengths
   int* ip = ctx_s + ((B + 3) & ~3);                           // [B + 1] item prefix
   int* tab_s = ip + ((B + 4) & ~3);                           // [B * MB] block table copy
@@ -167,6 +175,10 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
       mbar_init(&empty[s], NW);
     }
     mbar_init(setup, 1);
+    for (int k = 0; k < kFlushSlots; ++k) {
+      mbar_init(&fbar[k], NW);
+      mbar_init(&fempty[k], 1);
+    }
     fence_barrier_init();
     const uint32_t tx = (ctx_bulk ? (uint32_t)B * 4u : 0u) + (tab_in_smem ? (uint32_t)B * MB * 4u : 0u);
     if (tx) {
@@ -303,7 +315,59 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
     return;
   }
 
-  // ---- 3. compute warps (independent of each other) ----------------------------------
+  // ---- 3. flush warp: split-KV arrivals and merges ------------------------------------
+  if (warp == NW + 1) {
+    int k = 0;
+    uint32_t fph = 0;
+    for (;;) {
+      if (!mbar_wait_bounded(&fbar[k], fph, p.err)) {
+        flag[0] = 1;
+        return;
+      }
+      const int4 fm = fmeta[k];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&fempty[k]);  // the compute warps may refill slot k
+      if (++k == kFlushSlots) {
+        k = 0;
+        fph ^= 1;
+      }
+      if (fm.x < 0) break;
+      const int b = fm.x, i0 = ip[b], nitems = fm.z;
+      int last = 0;
+      if (lane == 0) {
+        __threadfence();  // the compute warps' partial stores (seen via fbar) before the arrival
+        int* cnt = p.counters + b;
+        last = (atomicAdd(cnt, 1) == nitems - 1);
+        if (last) *cnt = 0;  // every item of b has arrived; ready for the next call
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      __threadfence();
+      // combine: each lane covers dims 2*lane, 2*lane+1 (+64, ...) of every head
+      for (int h = 0; h < H; ++h) {
+        float M = -INFINITY;
+        for (int it = 0; it < nitems; ++it)
+          M = fmaxf(M, __ldcg(p.partials + ((size_t)(i0 + it) * H + h) * (D + 2) + D));
+        for (int d0 = 2 * lane; d0 < D; d0 += 64) {
+          float L = 0.f;
+          float2 o = make_float2(0.f, 0.f);
+          for (int it = 0; it < nitems; ++it) {
+            const float* sl = p.partials + ((size_t)(i0 + it) * H + h) * (D + 2);
+            const float w = exp2f(__ldcg(sl + D) - M);
+            L = fmaf(__ldcg(sl + D + 1), w, L);
+            o = __ffma2_rn(__ldcg(reinterpret_cast<const float2*>(sl + d0)), make_float2(w, w), o);
+          }
+          const float inv = 1.f / L;
+          T* orow = out + ((size_t)b * H + h) * D + d0;
+          orow[0] = Elem<T>::from_f(o.x * inv);
+          orow[1] = Elem<T>::from_f(o.y * inv);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---- 4. compute warps (independent of each other) ----------------------------------
   const int r = lane / LPR;    // q·k row of this lane
   const int sub = lane % LPR;  // which DPL-slice of the row
   const int rot = r & (NCH - 1);
@@ -316,6 +380,20 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
   int s = 0;
   uint32_t ph = 0;
   bool traced = false;
+  long long fseq = 0;  // items handed to the flush warp so far
+
+  // Hands item (b, item, nitems) — or the end marker b = -1 — to the flush warp.
+  auto hand_over = [&](int b, int item, int nitems) -> bool {
+    const int k = (int)(fseq % kFlushSlots);
+    if (fseq >= kFlushSlots &&
+        !mbar_wait_bounded(&fempty[k], (uint32_t)(((fseq / kFlushSlots) - 1) & 1), p.err))
+      return false;
+    if (warp == 0 && lane == 0) fmeta[k] = make_int4(b, item, nitems, 0);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&fbar[k]);
+    ++fseq;
+    return true;
+  };
 
   for (;;) {
     if (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&full[s], ph, p.err)) {
@@ -323,7 +401,10 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
       return;
     }
     const StageMeta mt = meta[s];
-    if (mt.b < 0) break;
+    if (mt.b < 0) {
+      if (!hand_over(-1, 0, 0)) flag[0] = 1;
+      break;
+    }
     if (tid == 0 && !traced) {
       SPD_TRACE(4);
       traced = true;
@@ -435,8 +516,8 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
     }
 
     if (!(mt.flags & kLast)) continue;
-    // ---- item end: this warp finishes its heads for (item, b) ---------------------------
-    const int i0 = ip[b], nitems = ip[b + 1] - ip[b];
+    // ---- item end: output, or partials handed to the flush warp --------------------------
+    const int nitems = ip[b + 1] - ip[b];
 #pragma unroll
     for (int k = 0; k < HPW; ++k) {
       const int h = warp * HPW + k;
@@ -449,10 +530,10 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
           acc[k][i].x += __shfl_xor_sync(0xffffffffu, acc[k][i].x, o);
           acc[k][i].y += __shfl_xor_sync(0xffffffffu, acc[k][i].y, o);
         }
-      T* orow = out + ((size_t)b * H + h) * D + cidx * VE;
       if (nitems == 1) {
         if (rg == 0) {
           const float inv = 1.f / ltot;
+          T* orow = out + ((size_t)b * H + h) * D + cidx * VE;
 #pragma unroll
           for (int i = 0; i < VE / 2; ++i) {
             orow[2 * i] = Elem<T>::from_f(acc[k][i].x * inv);
@@ -470,44 +551,10 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
         slot[D] = m[k];
         slot[D + 1] = ltot;
       }
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) {
-        __threadfence();
-        int* cnt = p.counters + (size_t)b * H + h;
-        last = (atomicAdd(cnt, 1) == nitems - 1);
-        if (last) {
-          *cnt = 0;  // every item of (b, h) has arrived; ready for the next call
-          __threadfence();
-        }
-      }
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (!last) continue;
-      __threadfence();  // every lane reads the other CTAs' partials after the arrival
-      float M = -INFINITY;
-      for (int it = 0; it < nitems; ++it)
-        M = fmaxf(M, __ldcg(p.partials + ((size_t)(i0 + it) * H + h) * (D + 2) + D));
-      float L = 0.f;
-      float2 o[VE / 2];
-#pragma unroll
-      for (int i = 0; i < VE / 2; ++i) o[i] = make_float2(0.f, 0.f);
-      for (int it = 0; it < nitems; ++it) {
-        const float* sl = p.partials + ((size_t)(i0 + it) * H + h) * (D + 2);
-        const float w = exp2f(__ldcg(sl + D) - M);
-        L = fmaf(__ldcg(sl + D + 1), w, L);
-        const float2 w2 = make_float2(w, w);
-#pragma unroll
-        for (int i = 0; i < VE / 2; ++i)
-          o[i] = __ffma2_rn(__ldcg(reinterpret_cast<const float2*>(sl + cidx * VE + 2 * i)), w2, o[i]);
-      }
-      if (rg == 0) {
-        const float inv = 1.f / L;
-#pragma unroll
-        for (int i = 0; i < VE / 2; ++i) {
-          orow[2 * i] = Elem<T>::from_f(o[i].x * inv);
-          orow[2 * i + 1] = Elem<T>::from_f(o[i].y * inv);
-        }
-      }
+    }
+    if (nitems > 1 && !hand_over(b, mt.item, nitems)) {
+      flag[0] = 1;
+      return;
     }
   }
   if (tid == 0) SPD_TRACE(5);
@@ -518,7 +565,7 @@ template <typename T, int D, int BS, int HPW>
 static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t stream) {
   PagedParams p = base;
   const int nw = (p.H + HPW - 1) / HPW;
-  const int threads = (nw + 1) * 32;
+  const int threads = (nw + 2) * 32;  // compute warps, producer warp, flush warp
   const size_t stage_bytes = ((size_t)2 * BS + 3) * p.H * D * sizeof(T);
   const size_t tab_bytes = (size_t)p.B * p.max_blocks * 4;
   p.table_in_smem = (tab_bytes <= kTableSmemMax && tab_bytes % 16 == 0 &&
@@ -533,7 +580,8 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
   if (S < 2 && 2 * stage_bytes + fixed <= 227 * 1024) S = 2;
   S = S < 1 ? 1 : (S > 8 ? 8 : S);
   p.stages = S;
-  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * ((size_t)S * 2 + 2) + 16 * (size_t)S + 16 +
+  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * ((size_t)S * 2 + 2) + 16 * kFlushSlots +
+                      16 * (size_t)S + 16 * kFlushSlots + 16 +
                       4 * ((((size_t)p.B + 3) & ~(size_t)3) + (((size_t)p.B + 4) & ~(size_t)3)) +
                       (p.table_in_smem ? tab_bytes : 0);
   if (smem > 227 * 1024) return SPD_ERR_UNSUPPORTED;
