@@ -29,11 +29,11 @@
 // * Compute warp w owns heads [w*HPW, (w+1)*HPW) and never synchronises with the other
 //   compute warps: it patches its own slice of an appended row; at the end of an item it
 //   writes the output (an item covering the whole sequence) or a partial (m, l, acc) to
-//   slot [item][h] and hands the item to the flush warp through a small mbarrier ring.
-// * The flush warp takes the latency of split-KV merging off the compute warps: per
-//   handed-over item it fences, bumps the sequence's arrival counter, and when it is the
-//   last arrival it combines the sequence's partials for all heads and resets the
-//   counter (no spinning, no second launch).
+//   slot [item][h].
+// * Split sequences are merged by a second, small kernel (one warp per (sequence, head),
+//   item-parallel loads) launched with programmatic dependent launch: the streaming
+//   kernel signals launch_dependents at its start, so the merge kernel's CTAs are already
+//   resident and waiting (griddepcontrol.wait) when the streaming kernel ends.
 // * q·k: 32/block_size lanes per row, q (pre-scaled by scale*log2 e) in registers, K
 //   chunks read in a per-row rotated order so the 8 lanes of a shared-memory phase hit
 //   distinct banks.  p·v: each lane owns one 16-byte chunk of a row.  Online softmax in
@@ -116,8 +116,6 @@ struct PagedGeom {
 };
 
 // Per-stage metadata written by the producer before it arms the stage.
-constexpr int kFlushSlots = 4;  // items in flight between compute warps and the flush warp
-
 struct StageMeta {
   int b;      // sequence, or -1: no more work
   int j;      // block index within the sequence
@@ -127,7 +125,7 @@ struct StageMeta {
 constexpr int kFirst = 1, kLast = 2;
 
 template <typename T, int D, int BS, int HPW>
-__global__ void __launch_bounds__(576) paged_decode_attn_kernel(const PagedParams p) {
+__global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParams p) {
   using Gm = PagedGeom<T, D, BS>;
   constexpr int LPR = Gm::LPR, DPL = Gm::DPL, CH = Gm::CH, NCH = Gm::NCH;
   constexpr int VE = Gm::VE, CPR = Gm::CPR, RG = Gm::RG, PVP = Gm::PVP;
@@ -145,11 +143,8 @@ __global__ void __launch_bounds__(576) paged_decode_attn_kernel(const PagedParam
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + round_up((size_t)S * stage_elems * sizeof(T), 128));
   uint64_t* empty = full + S;
   uint64_t* setup = empty + S;
-  uint64_t* fbar = setup + 2;                                 // [kFlushSlots] items handed over
-  uint64_t* fempty = fbar + kFlushSlots;                      // [kFlushSlots] slots free again
-  StageMeta* meta = reinterpret_cast<StageMeta*>(fempty + kFlushSlots);  // 16-byte aligned
-  int4* fmeta = reinterpret_cast<int4*>(meta + S);            // [kFlushSlots] {b, item, nitems, -}
-  int* flag = reinterpret_cast<int*>(fmeta + kFlushSlots);    // [0] abort, [1..3] spare
+  StageMeta* meta = reinterpret_cast<StageMeta*>(setup + 2);  // 16-byte aligned
+  int* flag = reinterpret_cast<int*>(meta + S);               // [0] abort, [1..3] spare
   int* ctx_s = flag + 4;                                      // [round4(B)] context lengths
   int* ip = ctx_s + ((B + 3) & ~3);                           // [B + 1] item prefix
   int* tab_s = ip + ((B + 4) & ~3);                           // [B * MB] block table copy
@@ -175,11 +170,10 @@ __global__ void __launch_bounds__(576) paged_decode_attn_kernel(const PagedParam
       mbar_init(&empty[s], NW);
     }
     mbar_init(setup, 1);
-    for (int k = 0; k < kFlushSlots; ++k) {
-      mbar_init(&fbar[k], NW);
-      mbar_init(&fempty[k], 1);
-    }
     fence_barrier_init();
+    // let the merge kernel that follows this launch get resident early; it waits for
+    // this grid to finish (griddepcontrol.wait) before it reads anything
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t tx = (ctx_bulk ? (uint32_t)B * 4u : 0u) + (tab_in_smem ? (uint32_t)B * MB * 4u : 0u);
     if (tx) {
       mbar_arrive_expect_tx(setup, tx);
@@ -315,59 +309,7 @@ __global__ void __launch_bounds__(576) paged_decode_attn_kernel(const PagedParam
     return;
   }
 
-  // ---- 3. flush warp: split-KV arrivals and merges ------------------------------------
-  if (warp == NW + 1) {
-    int k = 0;
-    uint32_t fph = 0;
-    for (;;) {
-      if (!mbar_wait_bounded(&fbar[k], fph, p.err)) {
-        flag[0] = 1;
-        return;
-      }
-      const int4 fm = fmeta[k];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&fempty[k]);  // the compute warps may refill slot k
-      if (++k == kFlushSlots) {
-        k = 0;
-        fph ^= 1;
-      }
-      if (fm.x < 0) break;
-      const int b = fm.x, i0 = ip[b], nitems = fm.z;
-      int last = 0;
-      if (lane == 0) {
-        __threadfence();  // the compute warps' partial stores (seen via fbar) before the arrival
-        int* cnt = p.counters + b;
-        last = (atomicAdd(cnt, 1) == nitems - 1);
-        if (last) *cnt = 0;  // every item of b has arrived; ready for the next call
-      }
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (!last) continue;
-      __threadfence();
-      // combine: each lane covers dims 2*lane, 2*lane+1 (+64, ...) of every head
-      for (int h = 0; h < H; ++h) {
-        float M = -INFINITY;
-        for (int it = 0; it < nitems; ++it)
-          M = fmaxf(M, __ldcg(p.partials + ((size_t)(i0 + it) * H + h) * (D + 2) + D));
-        for (int d0 = 2 * lane; d0 < D; d0 += 64) {
-          float L = 0.f;
-          float2 o = make_float2(0.f, 0.f);
-          for (int it = 0; it < nitems; ++it) {
-            const float* sl = p.partials + ((size_t)(i0 + it) * H + h) * (D + 2);
-            const float w = exp2f(__ldcg(sl + D) - M);
-            L = fmaf(__ldcg(sl + D + 1), w, L);
-            o = __ffma2_rn(__ldcg(reinterpret_cast<const float2*>(sl + d0)), make_float2(w, w), o);
-          }
-          const float inv = 1.f / L;
-          T* orow = out + ((size_t)b * H + h) * D + d0;
-          orow[0] = Elem<T>::from_f(o.x * inv);
-          orow[1] = Elem<T>::from_f(o.y * inv);
-        }
-      }
-    }
-    return;
-  }
-
-  // ---- 4. compute warps (independent of each other) ----------------------------------
+  // ---- 3. compute warps (independent of each other) ----------------------------------
   const int r = lane / LPR;    // q·k row of this lane
   const int sub = lane % LPR;  // which DPL-slice of the row
   const int rot = r & (NCH - 1);
@@ -380,31 +322,13 @@ __global__ void __launch_bounds__(576) paged_decode_attn_kernel(const PagedParam
   int s = 0;
   uint32_t ph = 0;
   bool traced = false;
-  long long fseq = 0;  // items handed to the flush warp so far
-
-  // Hands item (b, item, nitems) — or the end marker b = -1 — to the flush warp.
-  auto hand_over = [&](int b, int item, int nitems) -> bool {
-    const int k = (int)(fseq % kFlushSlots);
-    if (fseq >= kFlushSlots &&
-        !mbar_wait_bounded(&fempty[k], (uint32_t)(((fseq / kFlushSlots) - 1) & 1), p.err))
-      return false;
-    if (warp == 0 && lane == 0) fmeta[k] = make_int4(b, item, nitems, 0);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&fbar[k]);
-    ++fseq;
-    return true;
-  };
-
   for (;;) {
     if (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&full[s], ph, p.err)) {
       flag[0] = 1;
       return;
     }
     const StageMeta mt = meta[s];
-    if (mt.b < 0) {
-      if (!hand_over(-1, 0, 0)) flag[0] = 1;
-      break;
-    }
+    if (mt.b < 0) break;
     if (tid == 0 && !traced) {
       SPD_TRACE(4);
       traced = true;
@@ -516,7 +440,7 @@ __global__ void __launch_bounds__(576) paged_decode_attn_kernel(const PagedParam
     }
 
     if (!(mt.flags & kLast)) continue;
-    // ---- item end: output, or partials handed to the flush warp --------------------------
+    // ---- item end: the output, or a partial for the merge kernel --------------------------
     const int nitems = ip[b + 1] - ip[b];
 #pragma unroll
     for (int k = 0; k < HPW; ++k) {
@@ -552,20 +476,96 @@ __global__ void __launch_bounds__(576) paged_decode_attn_kernel(const PagedParam
         slot[D + 1] = ltot;
       }
     }
-    if (nitems > 1 && !hand_over(b, mt.item, nitems)) {
-      flag[0] = 1;
-      return;
-    }
   }
   if (tid == 0) SPD_TRACE(5);
 }
 
+// ------------------------------------------------------------------ merge kernel
+// One warp per (sequence, head) of a sequence that spans more than one item: reads the
+// items' partial (m, l, acc) in parallel (lane = item for m and l; all items' acc loads
+// issued before any is used) and writes acc_total / l_total.
+template <typename T, int D, int BS>
+__global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the streaming kernel has finished
+  const int lane = threadIdx.x & 31;
+  const long long pair = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (pair >= (long long)p.B * p.H) return;
+  const int b = (int)(pair / p.H), h = (int)(pair % p.H);
+  const int max_ctx = p.max_blocks * BS;
+  int i0 = 0, ctx_b = 0;
+  // item index of sequence b's first item = sum over b' < b of ceil(ceil(ctx/BS)/kItemUnits)
+  for (int bb = lane; bb <= b; bb += 32) {
+    int c = p.context_lens[bb];
+    c = c > max_ctx ? max_ctx : (c > 0 ? c : 0);
+    const int n = ((c + BS - 1) / BS + kItemUnits - 1) / kItemUnits;
+    if (bb < b) i0 += n;
+    else ctx_b = c;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    i0 += __shfl_xor_sync(0xffffffffu, i0, o);
+    ctx_b = max(ctx_b, __shfl_xor_sync(0xffffffffu, ctx_b, o));
+  }
+  const int nitems = ((ctx_b + BS - 1) / BS + kItemUnits - 1) / kItemUnits;
+  if (nitems <= 1) return;  // written by the streaming kernel (or zero)
+  const float* base = p.partials + ((size_t)i0 * p.H + h) * (D + 2);
+  const size_t stride = (size_t)p.H * (D + 2);  // next item, same head
+  float M = -INFINITY;
+  for (int it = lane; it < nitems; it += 32) M = fmaxf(M, __ldcg(base + it * stride + D));
+  M = warp_max(M);
+  float L = 0.f;
+  for (int it = lane; it < nitems; it += 32) L += __ldcg(base + it * stride + D + 1) * exp2f(__ldcg(base + it * stride + D) - M);
+  L = warp_sum(L);
+  const float inv = 1.f / L;
+  T* orow = reinterpret_cast<T*>(p.out) + ((size_t)b * p.H + h) * D;
+  for (int d0 = 2 * lane; d0 < D; d0 += 64) {
+    float2 o = make_float2(0.f, 0.f);
+    constexpr int U = 8;
+    for (int it0 = 0; it0 < nitems; it0 += U) {
+      float2 v[U];
+      float w[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {  // issue every load of this batch before using any
+        const int it = it0 + u;
+        if (it < nitems) {
+          v[u] = __ldcg(reinterpret_cast<const float2*>(base + it * stride + d0));
+          w[u] = __ldcg(base + it * stride + D);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (it0 + u < nitems) {
+          const float ww = exp2f(w[u] - M);
+          o = __ffma2_rn(v[u], make_float2(ww, ww), o);
+        }
+      }
+    }
+    orow[d0] = Elem<T>::from_f(o.x * inv);
+    if (d0 + 1 < D) orow[d0 + 1] = Elem<T>::from_f(o.y * inv);
+  }
+}
+
 // ------------------------------------------------------------------ host launcher
+template <typename T, int D, int BS>
+static int launch_merge(const PagedParams& p, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(((long long)p.B * p.H + 3) / 4));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, paged_merge_kernel<T, D, BS>, p) == cudaSuccess ? SPD_OK : SPD_ERR_CUDA;
+}
+
 template <typename T, int D, int BS, int HPW>
 static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t stream) {
   PagedParams p = base;
   const int nw = (p.H + HPW - 1) / HPW;
-  const int threads = (nw + 2) * 32;  // compute warps, producer warp, flush warp
+  const int threads = (nw + 1) * 32;  // compute warps + producer warp
   const size_t stage_bytes = ((size_t)2 * BS + 3) * p.H * D * sizeof(T);
   const size_t tab_bytes = (size_t)p.B * p.max_blocks * 4;
   p.table_in_smem = (tab_bytes <= kTableSmemMax && tab_bytes % 16 == 0 &&
@@ -580,8 +580,7 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
   if (S < 2 && 2 * stage_bytes + fixed <= 227 * 1024) S = 2;
   S = S < 1 ? 1 : (S > 8 ? 8 : S);
   p.stages = S;
-  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * ((size_t)S * 2 + 2) + 16 * kFlushSlots +
-                      16 * (size_t)S + 16 * kFlushSlots + 16 +
+  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * ((size_t)S * 2 + 2) + 16 * (size_t)S + 16 +
                       4 * ((((size_t)p.B + 3) & ~(size_t)3) + (((size_t)p.B + 4) & ~(size_t)3)) +
                       (p.table_in_smem ? tab_bytes : 0);
   if (smem > 227 * 1024) return SPD_ERR_UNSUPPORTED;
@@ -594,7 +593,8 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
     return SPD_ERR_CUDA;
   if (occ > kMaxCtasPerSm) occ = kMaxCtasPerSm;
   kfn<<<device_sms * occ, threads, smem, stream>>>(p);
-  return cudaPeekAtLastError() == cudaSuccess ? SPD_OK : SPD_ERR_CUDA;
+  if (cudaPeekAtLastError() != cudaSuccess) return SPD_ERR_CUDA;
+  return launch_merge<T, D, BS>(p, stream);
 }
 
 template <typename T, int D>
