@@ -162,8 +162,13 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
   if (tid == 0) SPD_TRACE(0);
   // ---- 1. set-up: barriers, bulk copies of lengths and table, first item take ------
   const bool ctx_bulk = ((B * 4) % 16 == 0) && ((reinterpret_cast<uintptr_t>(p.context_lens) & 15) == 0);
-  int first_item = 0;
   if (tid < 4) flag[tid] = 0;  // shared memory starts undefined
+  // Launched with programmatic dependent launch: this grid may become resident while the
+  // previous kernel in the stream still runs, so every thread waits for it before reading
+  // an input or writing an output.  Then the merge kernel that follows may get resident
+  // early; it waits for this grid to finish (griddepcontrol.wait) before reading anything.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -171,9 +176,6 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
     }
     mbar_init(setup, 1);
     fence_barrier_init();
-    // let the merge kernel that follows this launch get resident early; it waits for
-    // this grid to finish (griddepcontrol.wait) before it reads anything
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t tx = (ctx_bulk ? (uint32_t)B * 4u : 0u) + (tab_in_smem ? (uint32_t)B * MB * 4u : 0u);
     if (tx) {
       mbar_arrive_expect_tx(setup, tx);
@@ -183,7 +185,6 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
       mbar_arrive(setup);
     }
   }
-  if (warp == NW && lane == 0) first_item = atomicAdd(next_item, 1);  // overlaps the copies
   __syncthreads();
   if (!mbar_wait_bounded(setup, 0, p.err)) flag[0] = 1;
   if (!ctx_bulk) {
@@ -235,9 +236,11 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
       uint32_t ph = 0;
       long long n_issued = 0;
       bool alive = !flag[0];
-      int item = first_item;
+      // The first item of CTA c is c; later items come from the shared counter, offset by
+      // the grid size (no contended atomic before the first copy is issued).
+      int item = blockIdx.x;
       while (alive && item < n_items) {
-        const int nxt = atomicAdd(next_item, 1);  // next take, in flight while this item issues
+        const int nxt = (int)gridDim.x + atomicAdd(next_item, 1);  // next take, in flight meanwhile
         const int b = upper_index_i32(ip, B, item);
         const int nblk = (ctx_s[b] + BS - 1) / BS;
         const int j0 = (item - ip[b]) * kItemUnits;
@@ -487,6 +490,7 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
 template <typename T, int D, int BS>
 __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the streaming kernel has finished
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const long long pair = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (pair >= (long long)p.B * p.H) return;
@@ -592,8 +596,17 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kfn, threads, smem) != cudaSuccess || occ < 1)
     return SPD_ERR_CUDA;
   if (occ > kMaxCtasPerSm) occ = kMaxCtasPerSm;
-  kfn<<<device_sms * occ, threads, smem, stream>>>(p);
-  if (cudaPeekAtLastError() != cudaSuccess) return SPD_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(device_sms * occ));
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kfn, p) != cudaSuccess) return SPD_ERR_CUDA;
   return launch_merge<T, D, BS>(p, stream);
 }
 
