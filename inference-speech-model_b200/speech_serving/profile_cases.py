@@ -3,6 +3,7 @@
     python -m speech_serving.profile_cases paged_cfg2 --launches 3
     python -m speech_serving.profile_cases cross_cfg3 --launches 3
     python -m speech_serving.profile_cases proj_small --launches 3
+    python -m speech_serving.profile_cases cross_cfg3 --time 50   # CUDA-event timing
 
 Cases: paged_cfg2 = paged self-attention B=64 H=12 D=64 bs=16
 ctx~U[1,448] fp16; cross_cfg3 = cross-attention B=128 H=20 D=64 T=1500 valid~U[300,1500]
@@ -19,6 +20,9 @@ import torch
 from . import ops
 
 
+WORK = {}  # case -> (algorithmic bytes or flops per launch, unit)
+
+
 def _paged(dev, sets):
     g = torch.Generator().manual_seed(0)
     B, H, D, bs, NB = 64, 12, 64, 16, 4096
@@ -31,6 +35,7 @@ def _paged(dev, sets):
         vp = torch.randn(NB, bs, H, D, device=dev).half()
         out.append((q, kp, vp, tables.to(dev), ctx.to(dev)))
     ws = ops.paged_attn_workspace(B, H, D, 28, dev)
+    WORK["paged_cfg2"] = (sum(int(o[4].sum()) * H * D * 4 + 2 * B * H * D * 2 for o in out) / sets, "GB/s")
     return lambda i: ops.paged_decode_attention(*out[i % sets], scale=0.125, workspace=ws)
 
 
@@ -43,6 +48,7 @@ def _cross(dev, sets):
         out.append((torch.randn(B, H, D, device=dev).bfloat16(), torch.randn(B, H, T, D, device=dev).bfloat16(),
                     torch.randn(B, H, T, D, device=dev).bfloat16(), valid.to(dev)))
     ws = ops.cross_attn_workspace(B, H, D, dev)
+    WORK["cross_cfg3"] = (sum(int(o[3].sum()) * H * D * 4 + 2 * B * H * D * 2 for o in out) / sets, "GB/s")
     return lambda i: ops.cross_attention(*out[i % sets], scale=0.125, workspace=ws)
 
 
@@ -52,6 +58,7 @@ def _proj(dev, sets, d, L, H):
     w = (torch.randn(L * 2 * H * D, d, device=dev) * 0.02).bfloat16()
     b = torch.zeros(L * 2 * H * D, device=dev).bfloat16()
     out = torch.empty((1, L, 2, H, T, D), device=dev, dtype=torch.bfloat16)
+    WORK[f"proj_{d}"] = (2.0 * T * d * L * 2 * H * D, "TFLOP/s")
     return lambda i: ops.cross_kv_project(enc[i % sets], w, b, out)
 
 
@@ -68,6 +75,7 @@ def main():
     ap.add_argument("case", choices=sorted(CASES))
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--sets", type=int, default=2)
+    ap.add_argument("--time", type=int, default=0, help="time this many launches with CUDA events")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     run = CASES[a.case](dev, a.sets)
@@ -75,6 +83,21 @@ def main():
         run(i)
     torch.cuda.synchronize()
     print(f"{a.case}: {a.launches} launches ok")
+    if a.time:
+        for i in range(3):
+            run(i)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for i in range(a.time):
+            run(i)
+        e.record()
+        torch.cuda.synchronize()
+        us = s.elapsed_time(e) * 1000.0 / a.time
+        key = a.case if a.case in WORK else [k for k in WORK if k.startswith("proj")][0]
+        work, unit = WORK[key]
+        rate = work / (us * 1e-6) / (1e9 if unit == "GB/s" else 1e12)
+        print(f"{a.case}: {us:.2f} us per launch (plain stream launches), {rate:.1f} {unit}")
 
 
 if __name__ == "__main__":
