@@ -327,10 +327,14 @@ def run_ours(args):
     if rank != 0:
         return
     peak, peak_kind = _peaks()
+    # DRAM traffic per launch: the ncu capture's dram read+write over algorithmic bytes of
+    # the same kernel and shape (profiles/ncu_traffic.json), applied to this batch's bytes.
     traffic = None
     tf = REPO / "profiles" / "ncu_traffic.json"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get("paged_decode_attn_config2_bytes_per_launch")
+        ratio = json.loads(tf.read_text()).get("paged_decode_attn_config2", {}).get("traffic_over_algorithmic")
+        if ratio:
+            traffic = int(ratio * bytes_rank / args.steps)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
