@@ -200,7 +200,7 @@ def run_ours(args):
     world, rank, local = dist_setup(args)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    from speech_serving import ops
+    from speech_serving import ops, replicas
 
     c = CFG2
     sets = [make_inputs(1000 + 97 * rank + i, device=dev) for i in range(N_SETS)]
@@ -253,12 +253,9 @@ def run_ours(args):
             dist.barrier()
         sustain(0.6)
     ms = start.elapsed_time(end)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = replicas.max_over_ranks(ms)
     bytes_rank = sum(bytes_per[i % N_SETS] for i in range(args.steps))
-    value = bytes_rank * world / (ms_max / 1e3) / 1e9
+    value = replicas.whole_job_rate(replicas.sum_over_ranks(bytes_rank), ms_max) / 1e9
     launch_ms = ms / args.steps
     achieved = (bytes_rank / args.steps) / (launch_ms / 1e3) / 1e9
 
@@ -294,10 +291,8 @@ def run_ours(args):
             e2e_step(i)
         e1.record(stream)
     torch.cuda.synchronize()
-    et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(et, op=dist.ReduceOp.MAX)
-    e2e_value = bytes_rank * world / (float(et.item()) / 1e3) / 1e9
+    e2e_ms_max = replicas.max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = replicas.whole_job_rate(replicas.sum_over_ranks(bytes_rank), e2e_ms_max) / 1e9
     h2d = dq.numel() * 2 + dt_.numel() * 4 + dc.numel() * 4
     d2h = dout.numel() * 2
 

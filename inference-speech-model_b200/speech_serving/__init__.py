@@ -8,3 +8,7 @@ os.environ.setdefault("USE_TF", "0")
 os.environ.setdefault("TRANSFORMERS_NO_TF", "1")
 
 from . import ops  # noqa: E402,F401
+from .block_manager import BlockManager  # noqa: E402,F401
+from .dual_cache_manager import DualCacheManager  # noqa: E402,F401
+from .encoder_block_manager import EncoderBlockManager  # noqa: E402,F401
+from .memory_guard import MemoryGuard  # noqa: E402,F401

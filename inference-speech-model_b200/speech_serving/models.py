@@ -1,0 +1,375 @@
+"""Whisper-class encoder-decoder models whose single-token decode step runs on the B200
+decode kernels.
+
+``WhisperClassSpeechEncoderDecoderModel`` keeps the module structure and parameter names
+of the reference model (speech_serving/models.py:298-347 and DecoderLayer :79-108), so a
+seeded random init produces the same weights and reference state dicts load unchanged.
+``encode`` (:349-367) and the multi-token ``decode_step`` used for prompt prefill
+(:369-423) are plain PyTorch.  ``decode_step_paged`` is the hot path and replaces
+``decode_step_graph_fixed`` (:425-487): per layer it runs the paged self-attention
+kernel, which also writes the new token's K/V into its pool block (ops 1 + 3), then
+cross-attention straight from the graph-slot cross-KV buffer (op 2), with no bucket
+buffers and no masks.  It allocates no workspace and never syncs, so it can be
+captured in a CUDA graph.
+
+``PretrainedWhisperModel`` wraps a Hugging Face ``WhisperForConditionalGeneration``
+(reference :490-610).  It is built from a checkpoint or, without one, from a
+``WhisperConfig`` with random weights.  Its ``encode`` projects every decoder layer's
+cross K/V with ONE tcgen05 GEMM (op 4) into the graph-slot layout, and
+``decode_step_paged`` runs the HF decoder's arithmetic on the same kernels.
+"""
+from __future__ import annotations
+
+import math
+import os
+from typing import Any, List, Optional, Sequence, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+
+os.environ.setdefault("USE_TF", "0")
+
+
+class _LayerKV:
+    """Keys/values of one decoder layer ([B, H, T, D]), named like a DynamicCache layer."""
+
+    def __init__(self, keys: torch.Tensor, values: torch.Tensor):
+        self.keys, self.values = keys, values
+
+
+class KVCache:
+    """Per-layer keys/values returned by the multi-token ``decode_step`` (prefill)."""
+
+    def __init__(self, layers: Sequence[_LayerKV]):
+        self.layers = list(layers)
+
+
+class ModelOutput:
+    def __init__(self, logits: torch.Tensor, past_key_values: Optional[KVCache]):
+        self.logits = logits
+        self.past_key_values = past_key_values
+
+
+class DecoderLayer(nn.Module):
+    """Pre-norm transformer layer with self-attention, optional cross-attention and an
+    MLP; attribute names and creation order follow speech_serving/models.py:82-108."""
+
+    def __init__(self, hidden_dim: int, num_heads: int, head_dim: int, is_decoder: bool = True):
+        super().__init__()
+        self.hidden_dim, self.num_heads, self.head_dim, self.is_decoder = hidden_dim, num_heads, head_dim, is_decoder
+        inner = num_heads * head_dim
+        self.self_attn_q = nn.Linear(hidden_dim, inner, bias=False)
+        self.self_attn_k = nn.Linear(hidden_dim, inner, bias=False)
+        self.self_attn_v = nn.Linear(hidden_dim, inner, bias=False)
+        self.self_attn_out = nn.Linear(inner, hidden_dim, bias=False)
+        self.cross_attn_q = nn.Linear(hidden_dim, inner, bias=False)
+        self.cross_attn_k = nn.Linear(hidden_dim, inner, bias=False)
+        self.cross_attn_v = nn.Linear(hidden_dim, inner, bias=False)
+        self.cross_attn_out = nn.Linear(inner, hidden_dim, bias=False)
+        self.norm1 = nn.LayerNorm(hidden_dim)
+        self.norm2 = nn.LayerNorm(hidden_dim)
+        self.norm3 = nn.LayerNorm(hidden_dim)
+        self.mlp = nn.Sequential(nn.Linear(hidden_dim, hidden_dim * 4), nn.GELU(), nn.Linear(hidden_dim * 4, hidden_dim))
+
+    def _heads(self, t: torch.Tensor) -> torch.Tensor:  # [B, T, H*D] -> [B, H, T, D]
+        return t.view(t.shape[0], t.shape[1], self.num_heads, self.head_dim).transpose(1, 2)
+
+    def forward(self, x, past_key_values=None, encoder_hidden_states=None, encoder_past_kv=None, attention_mask=None,
+                encoder_attention_mask=None):
+        """Multi-token forward (encoder layers and decoder prefill), same arithmetic as the
+        reference's eager path (speech_serving/models.py:110-208)."""
+        B, T, _ = x.shape
+        neg = torch.finfo(x.dtype).min
+        h = self.norm1(x)
+        q, k, v = self._heads(self.self_attn_q(h)), self._heads(self.self_attn_k(h)), self._heads(self.self_attn_v(h))
+        if past_key_values is not None:
+            k = torch.cat([past_key_values[0].to(q.dtype), k], dim=2)
+            v = torch.cat([past_key_values[1].to(q.dtype), v], dim=2)
+        scale = 1.0 / math.sqrt(self.head_dim)
+        w = torch.matmul(q, k.transpose(-2, -1)) * scale
+        if attention_mask is not None:
+            m = attention_mask
+            m = m[:, None, None, :] if m.dim() == 2 else (m[:, None] if m.dim() == 3 else m)
+            if m.dtype == torch.bool:
+                w = w.masked_fill(~m, neg)
+            elif torch.isin(m, torch.tensor([0, 1], device=m.device)).all():
+                w = w.masked_fill(m == 0, neg)
+            else:
+                w = w + m.to(q.dtype)
+        if self.is_decoder and T > 1:
+            w = w + torch.triu(torch.full((T, k.shape[2]), float("-inf"), device=x.device, dtype=q.dtype), diagonal=1)
+        a = torch.matmul(F.softmax(w, dim=-1), v).transpose(1, 2).reshape(B, T, -1)
+        x = x + self.self_attn_out(a)
+        new_kv = (k, v)
+        cross = encoder_hidden_states is not None or encoder_past_kv is not None
+        if cross:
+            hc = self.norm2(x)
+            cq = self._heads(self.cross_attn_q(hc))
+            if encoder_past_kv is not None:
+                ck, cv = encoder_past_kv[0].to(cq.dtype), encoder_past_kv[1].to(cq.dtype)
+            else:
+                ck = self._heads(self.cross_attn_k(encoder_hidden_states))
+                cv = self._heads(self.cross_attn_v(encoder_hidden_states))
+            cw = torch.matmul(cq, ck.transpose(-2, -1)) * scale
+            if encoder_attention_mask is not None:
+                if encoder_attention_mask.dtype == torch.bool:
+                    cw = cw.masked_fill(~encoder_attention_mask, neg)
+                else:
+                    cw = cw + encoder_attention_mask.to(cq.dtype)
+            ca = torch.matmul(F.softmax(cw, dim=-1), cv).transpose(1, 2).reshape(B, T, -1)
+            x = x + self.cross_attn_out(ca)
+        x = x + self.mlp((self.norm3 if cross else self.norm2)(x))
+        return x, new_kv, None
+
+
+class WhisperClassSpeechEncoderDecoderModel(nn.Module):
+    """Random-init Whisper-class model; constructor and parameters as in the reference
+    (speech_serving/models.py:304-347)."""
+
+    def __init__(self, num_encoder_layers: int = 4, num_decoder_layers: int = 4, num_heads: int = 4,
+                 hidden_dim: int = 256, mel_dim: int = 80, vocab_size: int = 51200):
+        super().__init__()
+        self.num_encoder_layers, self.num_decoder_layers = num_encoder_layers, num_decoder_layers
+        self.num_heads, self.head_dim, self.hidden_dim = num_heads, hidden_dim // num_heads, hidden_dim
+        self.vocab_size = vocab_size
+        self.num_decoder_kv_heads = num_heads
+
+        class Config:
+            pass
+
+        self.config = Config()
+        self.config.num_hidden_layers = num_decoder_layers
+        self.config.num_attention_heads = num_heads
+        self.config.num_key_value_heads = num_heads
+        self.config.hidden_size = hidden_dim
+        self.config.vocab_size = vocab_size
+        self.config.encoder_num_layers = num_encoder_layers
+        self.conv1 = nn.Conv1d(mel_dim, hidden_dim, kernel_size=3, padding=1)
+        self.conv2 = nn.Conv1d(hidden_dim, hidden_dim, kernel_size=3, stride=2, padding=1)
+        self.encoder_layers = nn.ModuleList(
+            [DecoderLayer(hidden_dim, num_heads, self.head_dim, is_decoder=False) for _ in range(num_encoder_layers)])
+        self.encoder_norm = nn.LayerNorm(hidden_dim)
+        self.decoder_embed = nn.Embedding(vocab_size, hidden_dim)
+        self.decoder_layers = nn.ModuleList(
+            [DecoderLayer(hidden_dim, num_heads, self.head_dim, is_decoder=True) for _ in range(num_decoder_layers)])
+        self.decoder_norm = nn.LayerNorm(hidden_dim)
+        self.lm_head = nn.Linear(hidden_dim, vocab_size, bias=False)
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.decoder_norm.weight.dtype
+
+    def encode(self, mel_features: torch.Tensor) -> Tuple[torch.Tensor, List[Tuple[torch.Tensor, torch.Tensor]]]:
+        """[B, mel, frames] -> (hidden [B, T, d], per encoder layer (K, V) [B, H, T, D]).
+        The decoder's cross-attention reads encoder layer i's self-attention K/V."""
+        x = F.gelu(self.conv1(mel_features))
+        x = F.gelu(self.conv2(x)).transpose(1, 2)
+        kv = []
+        for layer in self.encoder_layers:
+            x, (k, v), _ = layer(x)
+            kv.append((k, v))
+        return self.encoder_norm(x), kv
+
+    def decode_step(self, input_ids, past_key_values=None, encoder_past_kv_list=None, encoder_hidden_states=None,
+                    attention_mask=None, encoder_attention_mask=None, position_ids=None, use_cache=True, **kwargs):
+        """Multi-token decoder forward (prompt prefill); returns logits and per-layer K/V."""
+        x = self.decoder_embed(input_ids).to(self.dtype)
+        layers = []
+        for i, layer in enumerate(self.decoder_layers):
+            past = None
+            if past_key_values is not None and i < len(past_key_values.layers):
+                past = (past_key_values.layers[i].keys, past_key_values.layers[i].values)
+            enc = encoder_past_kv_list[i] if encoder_past_kv_list is not None and i < len(encoder_past_kv_list) else None
+            x, (k, v), _ = layer(x, past_key_values=past, encoder_hidden_states=None if enc is not None else
+                                 encoder_hidden_states, encoder_past_kv=enc, attention_mask=attention_mask,
+                                 encoder_attention_mask=encoder_attention_mask)
+            layers.append(_LayerKV(k, v))
+        return ModelOutput(self.lm_head(self.decoder_norm(x)), KVCache(layers) if use_cache else None)
+
+    # ---- decode hot path -------------------------------------------------------------
+    def cross_kv_from_encoder(self, encoder_kv_list, slots: torch.Tensor, slot: int) -> int:
+        """Copies one request's encoder K/V (direct handoff) into graph slot ``slot`` of
+        ``slots`` [S, L, 2, H, T, D]; returns the encoder length."""
+        T = encoder_kv_list[0][0].shape[2]
+        for l, (k, v) in enumerate(encoder_kv_list):
+            slots[slot, l, 0, :, :T].copy_(k[0])
+            slots[slot, l, 1, :, :T].copy_(v[0])
+        return T
+
+    def decode_step_paged(self, st, n: int) -> torch.Tensor:
+        """One decode step for slots [0, n) of the paged decode state ``st``
+        (graph_decode_buffers.PagedDecodeState): tokens st.token_ids[:n], attended lengths
+        st.ctx_lens[:n] (including the new token; 0 = inactive slot), block tables
+        st.block_tables[:n], cross K/V st.cross_kv[:n] with lengths st.cross_lens[:n].
+        Returns the greedy next tokens [n] (int64)."""
+        x = self.decoder_embed(st.token_ids[:n]).to(self.dtype)  # [n, d]
+        H, D = self.num_heads, self.head_dim
+        scale = 1.0 / math.sqrt(D)
+        for l, layer in enumerate(self.decoder_layers):
+            h = layer.norm1(x)
+            q = layer.self_attn_q(h).view(n, H, D)
+            k = layer.self_attn_k(h).view(n, H, D)
+            v = layer.self_attn_v(h).view(n, H, D)
+            a = ops.paged_decode_attention(q, st.key_pool[l], st.value_pool[l], st.block_tables[:n], st.ctx_lens[:n],
+                                           scale=scale, k_new=k, v_new=v, workspace=st.paged_ws[n])
+            x = x + layer.self_attn_out(a.view(n, -1))
+            cq = layer.cross_attn_q(layer.norm2(x)).view(n, H, D)
+            c = ops.cross_attention(cq, st.cross_kv[:n, l, 0], st.cross_kv[:n, l, 1], st.cross_lens[:n], scale=scale,
+                                    workspace=st.cross_ws[n])
+            x = x + layer.cross_attn_out(c.view(n, -1))
+            x = x + layer.mlp(layer.norm3(x))
+        logits = self.lm_head(self.decoder_norm(x))
+        return torch.argmax(logits, dim=-1)
+
+
+class PretrainedWhisperModel(nn.Module):
+    """Hugging Face Whisper wrapper (reference speech_serving/models.py:490-610).
+
+    Build it from ``model_name_or_path`` (a local checkpoint) or, with no checkpoint at
+    hand, from ``config`` (a ``WhisperConfig``) with random weights drawn under
+    ``seed``."""
+
+    def __init__(self, model_name_or_path: Optional[str] = None, device: str = "cuda",
+                 dtype: torch.dtype = torch.float16, local_files_only: bool = True, config: Any = None,
+                 seed: int = 0):
+        from transformers import WhisperForConditionalGeneration
+
+        if isinstance(dtype, str):
+            dtype = getattr(torch, dtype)
+        super().__init__()
+        self.device, self.dtype_ = device, dtype
+        if config is not None:
+            torch.manual_seed(seed)
+            hf = WhisperForConditionalGeneration(config)
+        else:
+            hf = WhisperForConditionalGeneration.from_pretrained(model_name_or_path, dtype=dtype,
+                                                                 local_files_only=local_files_only)
+        self.hf_model = hf.to(device=device, dtype=dtype).eval()
+        cfg = self.hf_model.config
+        self.config = cfg
+        self.num_encoder_layers, self.num_decoder_layers = cfg.encoder_layers, cfg.decoder_layers
+        self.num_heads = cfg.decoder_attention_heads
+        self.num_decoder_kv_heads = self.num_encoder_kv_heads = self.num_heads
+        self.head_dim = cfg.d_model // self.num_heads
+        self.hidden_dim, self.vocab_size = cfg.d_model, cfg.vocab_size
+        suppress = getattr(cfg, "suppress_tokens", None)
+        if suppress:
+            m = torch.zeros(self.vocab_size, dtype=torch.bool, device=device)
+            m[list(suppress)] = True
+            self.register_buffer("suppress_mask", m)
+        else:
+            self.suppress_mask = None
+        self._w_kv = None
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.dtype_
+
+    def stacked_cross_kv_weights(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        if self._w_kv is None:
+            self._w_kv = ops.stack_cross_kv_weights(self.hf_model.model.decoder.layers)
+        return self._w_kv
+
+    def encode(self, mel_features: torch.Tensor, out_slots: Optional[torch.Tensor] = None,
+               slot_ids: Optional[torch.Tensor] = None):
+        """Encoder forward, then every decoder layer's cross K/V by one GEMM (op 4).
+
+        Without ``out_slots`` a [B, L, 2, H, T, D] buffer is allocated and the return
+        value matches the reference: (enc_out, [(K, V)] per layer, K/V [B, H, T, D]).
+        With ``out_slots`` ([S, L, 2, H, T_out, D]) the projections are written straight
+        into slots ``slot_ids``."""
+        enc_out = self.hf_model.model.encoder(mel_features.to(self.dtype)).last_hidden_state.contiguous()
+        B, T, d = enc_out.shape
+        L, H, D = self.num_decoder_layers, self.num_heads, self.head_dim
+        if self.dtype not in (torch.float16, torch.bfloat16):
+            # the tcgen05 projection takes 16-bit operands; fp32 models project per layer
+            # with their own k_proj / v_proj, as the reference does (models.py:554-561)
+            kv = []
+            for l, layer in enumerate(self.hf_model.model.decoder.layers):
+                att = layer.encoder_attn
+                k = att.k_proj(enc_out).view(B, T, H, D).transpose(1, 2)
+                v = att.v_proj(enc_out).view(B, T, H, D).transpose(1, 2)
+                if out_slots is not None:
+                    idx = slot_ids.long() if slot_ids is not None else torch.arange(B, device=enc_out.device)
+                    out_slots[idx, l, 0, :, :T] = k
+                    out_slots[idx, l, 1, :, :T] = v
+                kv.append((k, v))
+            return enc_out, kv
+        w, b = self.stacked_cross_kv_weights()
+        if out_slots is None:
+            out_slots = torch.empty((B, L, 2, H, T, D), dtype=self.dtype, device=enc_out.device)
+            slot_ids = None
+        ops.cross_kv_project(enc_out, w, b, out_slots, slot_ids=slot_ids)
+        if slot_ids is None:
+            kv = [(out_slots[:B, l, 0, :, :T], out_slots[:B, l, 1, :, :T]) for l in range(L)]
+        else:
+            kv = [(out_slots[slot_ids.long(), l, 0, :, :T], out_slots[slot_ids.long(), l, 1, :, :T]) for l in range(L)]
+        return enc_out, kv
+
+    def cross_kv_from_encoder(self, encoder_kv_list, slots: torch.Tensor, slot: int) -> int:
+        T = encoder_kv_list[0][0].shape[2]
+        for l, (k, v) in enumerate(encoder_kv_list):
+            slots[slot, l, 0, :, :T].copy_(k[0])
+            slots[slot, l, 1, :, :T].copy_(v[0])
+        return T
+
+    def decode_step(self, input_ids, past_key_values=None, encoder_past_kv_list=None, encoder_hidden_states=None,
+                    attention_mask=None, encoder_attention_mask=None, position_ids=None, use_cache=True, **kwargs):
+        """Multi-token HF decoder forward (prompt prefill), cross K/V from the encoder's
+        projections (reference speech_serving/models.py:563-610)."""
+        from transformers.cache_utils import DynamicCache, EncoderDecoderCache
+
+        B = input_ids.shape[0]
+        T = encoder_past_kv_list[0][0].shape[2] if encoder_past_kv_list is not None else 1500
+        cross = DynamicCache()
+        if encoder_past_kv_list is not None:
+            for l, (k, v) in enumerate(encoder_past_kv_list):
+                cross.update(k.contiguous(), v.contiguous(), layer_idx=l)
+        selfc = DynamicCache()
+        if past_key_values is not None:
+            for l, lay in enumerate(past_key_values.layers):
+                selfc.update(lay.keys, lay.values, layer_idx=l)
+        cache = EncoderDecoderCache(selfc, cross)
+        for l in range(len(cross.layers)):
+            cache.is_updated[l] = True
+        dummy = torch.empty((B, T, self.hidden_dim), device=input_ids.device, dtype=self.dtype)
+        out = self.hf_model.model.decoder(input_ids=input_ids, encoder_hidden_states=dummy, past_key_values=cache,
+                                          attention_mask=attention_mask, position_ids=position_ids, use_cache=True)
+        logits = self.hf_model.proj_out(out.last_hidden_state)
+        if self.suppress_mask is not None:
+            logits = logits.masked_fill(self.suppress_mask, float("-inf"))
+        sc = out.past_key_values.self_attention_cache
+        layers = [_LayerKV(sc.layers[l].keys, sc.layers[l].values) for l in range(self.num_decoder_layers)]
+        return ModelOutput(logits, KVCache(layers) if use_cache else None)
+
+    def decode_step_paged(self, st, n: int) -> torch.Tensor:
+        """One HF-Whisper decode step for slots [0, n) on the paged kernels (same contract
+        as WhisperClassSpeechEncoderDecoderModel.decode_step_paged).  Query scaling
+        follows WhisperAttention: q = q_proj(h) * head_dim**-0.5, attention scale 1."""
+        dec = self.hf_model.model.decoder
+        H, D = self.num_heads, self.head_dim
+        pos = (st.ctx_lens[:n] - 1).clamp_(min=0).long()
+        x = dec.embed_tokens(st.token_ids[:n]) * dec.embed_scale + dec.embed_positions.weight[pos]
+        for l, layer in enumerate(dec.layers):
+            sa = layer.self_attn
+            h = layer.self_attn_layer_norm(x)
+            q = (sa.q_proj(h) * sa.scaling).view(n, H, D)
+            k = sa.k_proj(h).view(n, H, D)
+            v = sa.v_proj(h).view(n, H, D)
+            a = ops.paged_decode_attention(q, st.key_pool[l], st.value_pool[l], st.block_tables[:n], st.ctx_lens[:n],
+                                           scale=1.0, k_new=k, v_new=v, workspace=st.paged_ws[n])
+            x = x + sa.out_proj(a.view(n, -1))
+            ea = layer.encoder_attn
+            cq = (ea.q_proj(layer.encoder_attn_layer_norm(x)) * ea.scaling).view(n, H, D)
+            c = ops.cross_attention(cq, st.cross_kv[:n, l, 0], st.cross_kv[:n, l, 1], st.cross_lens[:n], scale=1.0,
+                                    workspace=st.cross_ws[n])
+            x = x + ea.out_proj(c.view(n, -1))
+            h = layer.final_layer_norm(x)
+            x = x + layer.fc2(layer.activation_fn(layer.fc1(h)))
+        logits = self.hf_model.proj_out(dec.layer_norm(x))
+        if self.suppress_mask is not None:
+            logits = logits.masked_fill(self.suppress_mask, float("-inf"))
+        return torch.argmax(logits, dim=-1)
