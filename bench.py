@@ -193,6 +193,109 @@ def run_reference(args):
     print(json.dumps(line))
 
 
+# ---------------------------------------------------------------------------- serving legs
+SERVING = {
+    "config1": dict(arch="whisper-class-tiny", dtype="float32", n=4, rate=None, out=(64, 64), mels=80,
+                    desc="WhisperClassSpeechEncoderDecoderModel(4,4,6,384,80,51865) seed 0, fp32, 4 requests, "
+                         "64 tokens each, graph decode, direct handoff"),
+    "config4": dict(arch="whisper-small", dtype="float16", n=256, rate=None, out=(20, 200), mels=80,
+                    desc="random-init Whisper-small, fp16, 256-request burst, audio U[2,30] s, outputs U{20..200}"),
+    "config5": dict(arch="whisper-large-v3", dtype="bfloat16", n=2048, rate=64.0, out=(20, 224), mels=128,
+                    desc="random-init Whisper-large-v3, bf16, Poisson 64 req/s per GPU, audio U[2,30] s, "
+                         "outputs U{20..224}"),
+}
+
+
+def _serving_model(cfg, dev):
+    import torch
+    from speech_serving.models import PretrainedWhisperModel, WhisperClassSpeechEncoderDecoderModel
+    from speech_serving.serving import whisper_config
+
+    dtype = getattr(torch, cfg["dtype"])
+    if cfg["arch"] == "whisper-class-tiny":
+        torch.manual_seed(0)
+        return WhisperClassSpeechEncoderDecoderModel(4, 4, 6, 384, 80, 51865).to(dev, dtype).eval(), dtype
+    return PretrainedWhisperModel(config=whisper_config(cfg["arch"]), device=str(dev), dtype=dtype, seed=0), dtype
+
+
+def _serving_scheduler(model, dtype, dev, max_batch=64, dec_blocks=4096):
+    from speech_serving import BlockManager, DualCacheManager, EncoderBlockManager, MemoryGuard
+    from speech_serving.phase_aware_scheduler import PhaseAwareSpeechScheduler
+
+    L, H, D = model.num_decoder_layers, model.num_heads, model.head_dim
+    enc = EncoderBlockManager(L, H, D, 16, 1, dtype=dtype, device=str(dev))  # direct handoff: unused
+    dec = BlockManager(L, H, D, 16, dec_blocks, dtype=dtype, device=str(dev))
+    return PhaseAwareSpeechScheduler(model, DualCacheManager(enc, dec), MemoryGuard(), max_batch_size=max_batch,
+                                     device=str(dev), eos_token_id=-1, batch_encoder=True, graph_decode=True,
+                                     graph_readback_k=4, graph_direct_encoder_kv=True)
+
+
+def serving_leg(name, n_req, dev, rank, world):
+    """Decoder tokens/s of one serving configuration: every rank serves its own request
+    stream (replicas); whole-job tokens/s = tokens of all ranks / slowest rank's wall."""
+    import torch
+    import torch.distributed as dist
+    from speech_serving import replicas
+    from speech_serving.phase_aware_scheduler import WHISPER_DEFAULT_PREFIX_TOKENS
+    from speech_serving.serving import run_engine, synthetic_requests
+
+    cfg = SERVING[name]
+    model, dtype = _serving_model(cfg, dev)
+    sched = _serving_scheduler(model, dtype, dev, max_batch=min(64, max(4, n_req)))
+    if name == "config1":
+        gen = torch.Generator().manual_seed(1)
+        from speech_serving.serving import SyntheticRequest
+        reqs = [SyntheticRequest(torch.randn(80, 3000, generator=gen).clamp(-1.5, 1.5).pin_memory(), 30.0, 64, 0.0)
+                for _ in range(4)]
+        warm = reqs
+    else:
+        reqs = synthetic_requests(n_req, cfg["mels"], seed=1000 + rank, out_lo=cfg["out"][0], out_hi=cfg["out"][1],
+                                  rate=cfg["rate"])
+        warm = synthetic_requests(8, cfg["mels"], seed=99, out_lo=8, out_hi=16)
+    run_engine(sched, warm, WHISPER_DEFAULT_PREFIX_TOKENS)  # captures the graphs
+    sched.reset_telemetry()
+    if world > 1:
+        dist.barrier()
+    r = run_engine(sched, reqs, WHISPER_DEFAULT_PREFIX_TOKENS)
+    wall_max = replicas.max_over_ranks(r["wall_s"])
+    toks_all = replicas.sum_over_ranks(r["generated_tokens"])
+    leaks = sched.dual_cache.decoder_bm.allocated_block_count
+    out = {"workload": cfg["desc"], "requests_per_rank": r["requests"], "failed": r["failed"],
+           "decoder_tok_s": round(replicas.whole_job_rate(toks_all, wall_max * 1e3), 1),
+           "generated_tokens": int(toks_all), "wall_s_max": round(wall_max, 3),
+           "rank0": {k: r[k] for k in ("decoder_tok_s", "decode_steps", "decode_phase_s", "ttft_p50_s",
+                                       "latency_p50_s", "latency_p95_s")},
+           "leaked_decoder_blocks": leaks, "timing": "wall clock around the serving loop, synchronized both ends"}
+    if name == "config1":
+        out["tokens"] = [q.generated_tokens for q in sorted(sched.completed, key=lambda q: q.id)]
+    del sched, model
+    torch.cuda.empty_cache()
+    return out
+
+
+def serving_cpu_baseline():
+    """Config 1 through the CPU eager-decode oracle (the reference's eager arithmetic) on
+    all host cores: decoder tokens/s."""
+    import torch
+    from oracle import eager_decode
+    from speech_serving.models import WhisperClassSpeechEncoderDecoderModel
+    from speech_serving.phase_aware_scheduler import WHISPER_DEFAULT_PREFIX_TOKENS
+
+    threads = os.cpu_count()
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    sd = WhisperClassSpeechEncoderDecoderModel(4, 4, 6, 384, 80, 51865).state_dict()
+    gen = torch.Generator().manual_seed(1)
+    mels = torch.stack([torch.randn(80, 3000, generator=gen).clamp(-1.5, 1.5) for _ in range(4)])
+    t0 = time.perf_counter()
+    toks = eager_decode.greedy_decode(sd, mels, WHISPER_DEFAULT_PREFIX_TOKENS, 64, num_heads=6)
+    dt = time.perf_counter() - t0
+    n = sum(len(t) for t in toks)
+    return {"value": round(n / dt, 1), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"config 1 end to end (encode + 4x64 greedy tokens) in {dt:.2f} s, oracle/eager_decode.py",
+            "tokens": toks}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -315,9 +418,23 @@ def run_ours(args):
         if ops.read_error_word(ws) != 0:
             raise RuntimeError("kernel reported a device error during the benchmark")
 
+    del graph
+    serving = {}
+    legs = [x for x in args.serving.split(",") if x and x != "none"]
+    for name in legs:
+        n_req = {"config1": 4, "config4": SERVING["config4"]["n"], "config5": args.config5_requests}[name]
+        serving[name] = serving_leg(name, n_req, dev, rank, world)
+    if rank == 0 and world == 1 and "config1" in serving and not args.no_cpu_baseline:
+        cb = serving_cpu_baseline()
+        ours = serving["config1"].pop("tokens")
+        ref = cb.pop("tokens")
+        agree = sum(a == b for x, y in zip(ours, ref) for a, b in zip(x, y)) / max(1, sum(len(x) for x in ref))
+        serving["config1"]["cpu_baseline"] = cb
+        serving["config1"]["token_agreement_vs_cpu_oracle"] = round(agree, 4)
+    elif "config1" in serving:
+        serving["config1"].pop("tokens", None)
     if world > 1:
         dist.barrier()
-        del graph
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -346,9 +463,10 @@ def run_ours(args):
                      "bytes_per_launch": int(bytes_rank / args.steps), "launch_us": round(launch_ms * 1e3, 3)},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "speech_serving.ops.paged_decode_attention (ctypes -> C ABI), pinned host buffers"},
-        "gpu_launches": args.steps,
+        "gpu_launches": 2 * args.steps,  # streaming kernel + split merge kernel per step
         "clocks": sampler.summary(),
         "max_abs_err_vs_oracle": ok_err,
+        "serving": serving,
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
@@ -363,6 +481,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--serving", default="config1,config4,config5",
+                    help="comma-separated serving legs (config1, config4, config5) or none")
+    ap.add_argument("--config5-requests", type=int, default=256,
+                    help="config-5 requests per rank (a bounded sample of the 2048-request stream)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -264,6 +264,9 @@ class PretrainedWhisperModel(nn.Module):
             self.suppress_mask = None
         self._w_kv = None
 
+    # encode() can write the cross K/V straight into graph slots (direct handoff)
+    encodes_into_slots = True
+
     @property
     def dtype(self) -> torch.dtype:
         return self.dtype_
@@ -279,8 +282,8 @@ class PretrainedWhisperModel(nn.Module):
 
         Without ``out_slots`` a [B, L, 2, H, T, D] buffer is allocated and the return
         value matches the reference: (enc_out, [(K, V)] per layer, K/V [B, H, T, D]).
-        With ``out_slots`` ([S, L, 2, H, T_out, D]) the projections are written straight
-        into slots ``slot_ids``."""
+        With ``out_slots`` ([S, L, 2, H, T_out, D]) and ``slot_ids`` (int32 [B]) the
+        projections are written straight into those slots and the K/V list is None."""
         enc_out = self.hf_model.model.encoder(mel_features.to(self.dtype)).last_hidden_state.contiguous()
         B, T, d = enc_out.shape
         L, H, D = self.num_decoder_layers, self.num_heads, self.head_dim
@@ -297,17 +300,15 @@ class PretrainedWhisperModel(nn.Module):
                     out_slots[idx, l, 0, :, :T] = k
                     out_slots[idx, l, 1, :, :T] = v
                 kv.append((k, v))
-            return enc_out, kv
+            return enc_out, (None if slot_ids is not None else kv)
         w, b = self.stacked_cross_kv_weights()
         if out_slots is None:
             out_slots = torch.empty((B, L, 2, H, T, D), dtype=self.dtype, device=enc_out.device)
             slot_ids = None
         ops.cross_kv_project(enc_out, w, b, out_slots, slot_ids=slot_ids)
-        if slot_ids is None:
-            kv = [(out_slots[:B, l, 0, :, :T], out_slots[:B, l, 1, :, :T]) for l in range(L)]
-        else:
-            kv = [(out_slots[slot_ids.long(), l, 0, :, :T], out_slots[slot_ids.long(), l, 1, :, :T]) for l in range(L)]
-        return enc_out, kv
+        if slot_ids is not None:
+            return enc_out, None
+        return enc_out, [(out_slots[:B, l, 0, :, :T], out_slots[:B, l, 1, :, :T]) for l in range(L)]
 
     def cross_kv_from_encoder(self, encoder_kv_list, slots: torch.Tensor, slot: int) -> int:
         T = encoder_kv_list[0][0].shape[2]

@@ -298,11 +298,12 @@ class PhaseAwareSpeechScheduler:
                                     for r in batch]).to(self.device)
                 t0 = time.perf_counter()
                 with self.phase_timer.measure(batch, "encoder_forward"), torch.no_grad():
-                    hidden, kv = self.model.encode(mels)
+                    hidden, kv = self._encode(batch, mels)
                 enc_time = time.perf_counter() - t0
                 self.encoder_calls += 1
                 for i, r in enumerate(batch):
-                    self._setup_safely(r, hidden[i:i + 1], [(k[i:i + 1], v[i:i + 1]) for k, v in kv], None, enc_time)
+                    self._setup_safely(r, hidden[i:i + 1], None if kv is None else
+                                       [(k[i:i + 1], v[i:i + 1]) for k, v in kv], None, enc_time)
                 return
             if batch:
                 self.queue.insert(0, batch[0])
@@ -338,13 +339,30 @@ class PhaseAwareSpeechScheduler:
                 else:
                     t0 = time.perf_counter()
                     with self.phase_timer.measure([req], "encoder_forward"), torch.no_grad():
-                        hidden, kv = self.model.encode(mel_in)
+                        hidden, kv = self._encode([req], mel_in)
                     enc_time = time.perf_counter() - t0
                     self.encoder_calls += 1
                     self._setup_request_after_encode(req, hidden, kv, full_hash, enc_time)
             except Exception as e:
                 logger.error(f"Error in ENCODE_PHASE for req {req.id}: {e}", exc_info=True)
                 self._complete_request(req, status=RequestPhase.FAILED)
+
+    def _reserve_slot(self, req: DualCacheRequest) -> int:
+        buf = self.graph_buffers
+        slot = buf.reserve_slot()
+        req.slot_idx = req.graph_slot_idx = slot
+        req.graph_slot_reused = buf.slots[slot].reused
+        return slot
+
+    def _encode(self, reqs: List[DualCacheRequest], mels: torch.Tensor):
+        """Encoder forward.  With direct handoff and a model whose projection can target
+        the graph slots, each request's slot is reserved first and the cross K/V are
+        written straight into it (no K/V list is returned then)."""
+        if self.graph_direct_encoder_kv and getattr(self.model, "encodes_into_slots", False):
+            slots = [self._reserve_slot(r) for r in reqs]
+            ids = torch.tensor(slots, dtype=torch.int32).to(self.graph_buffers.device, non_blocking=True)
+            return self.model.encode(mels, out_slots=self.graph_buffers.cross_kv, slot_ids=ids)
+        return self.model.encode(mels)
 
     def _setup_safely(self, req, hidden, kv, full_hash, enc_time) -> None:
         try:
@@ -359,9 +377,7 @@ class PhaseAwareSpeechScheduler:
                                     hit_entry: Optional[Dict[str, Any]] = None) -> None:
         enc_bm, dec_bm = self.dual_cache.encoder_bm, self.dual_cache.decoder_bm
         buf = self.graph_buffers
-        slot = buf.reserve_slot()
-        req.slot_idx = req.graph_slot_idx = slot
-        req.graph_slot_reused = buf.slots[slot].reused
+        slot = req.slot_idx if req.slot_idx is not None else self._reserve_slot(req)
         dev = buf.device
         if hit_entry is not None:
             enc_len = hit_entry["enc_seq_len"]
@@ -372,8 +388,9 @@ class PhaseAwareSpeechScheduler:
         L = min(len(encoder_kv_list) if encoder_kv_list is not None else enc_bm.num_layers, buf.num_decoder_layers)
 
         if self.graph_direct_encoder_kv:
-            with self.phase_timer.measure([req], "cross_kv_contiguous_or_graph_copy"):
-                buf.model.cross_kv_from_encoder(encoder_kv_list, buf.cross_kv, slot)
+            if encoder_kv_list is not None:  # else the encoder already wrote the slot
+                with self.phase_timer.measure([req], "cross_kv_contiguous_or_graph_copy"):
+                    buf.model.cross_kv_from_encoder(encoder_kv_list, buf.cross_kv, slot)
         else:
             if hit_entry is None:
                 with self.phase_timer.measure([req], "block_allocate"):

@@ -102,3 +102,24 @@ def test_oracle_flags_planted_mistake():
     good = O.paged_decode_attention(q, kp, vp, np.array([[0, 1]], np.int32), np.array([12], np.int32))
     bad = O.paged_decode_attention(q, kp, vp, np.array([[0, 2]], np.int32), np.array([12], np.int32))
     assert np.abs(good - bad).max() > 1e-3
+
+
+def test_eager_decode_oracle_reproduces_reference_config1(golden_dir):
+    """The CPU eager-decode oracle, given the seed-0 weights of the config-1 model,
+    reproduces the reference scheduler's greedy tokens (tests/golden/config1_tokens.json)."""
+    import json
+
+    import torch
+
+    from oracle import eager_decode
+    from speech_serving.models import WhisperClassSpeechEncoderDecoderModel
+
+    g = json.loads((golden_dir / "config1_tokens.json").read_text())
+    torch.manual_seed(0)
+    sd = WhisperClassSpeechEncoderDecoderModel(4, 4, 6, 384, 80, 51865).state_dict()
+    gen = torch.Generator().manual_seed(1)
+    mels = torch.stack([torch.randn(80, 3000, generator=gen).clamp(-1.5, 1.5) for _ in range(4)])
+    got = eager_decode.greedy_decode(sd, mels, g["prompt"], g["max_new_tokens"], num_heads=6)
+    n = sum(len(t) for t in g["tokens"])
+    agree = sum(a == b for ga, gb in zip(got, g["tokens"]) for a, b in zip(ga, gb))
+    assert agree / n >= 0.99
