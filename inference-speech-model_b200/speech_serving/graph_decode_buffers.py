@@ -15,7 +15,11 @@ a paged kernel:
   handed out lowest-first.
 * Per step the host uploads nothing.  Tokens and lengths advance on the device inside
   the graph; only slot assignment/release touch device state (stream-ordered
-  non-blocking copies).  New tokens are copied into a pinned host ring after each
+  non-blocking copies).
+* Prompt prefill can be folded into the graph: a slot assigned with its prompt starts at
+  position 0 and, while its position is inside the prompt, the step feeds the next prompt
+  token instead of the argmax.  Each prompt token's K/V is written by the fused append of
+  the paged kernel; the outputs of the first P-1 steps are dropped at readback.  New tokens are copied into a pinned host ring after each
   replay and read back every `readback_k` steps (:586-621).
 * Cross K/V of the slots live in one [S, L, 2, H, T_max, D] buffer, filled once at
   handoff (direct copy, block gather, or the projection GEMM writing straight into it).
@@ -33,6 +37,7 @@ BATCH_BUCKETS = [1, 2, 4, 8, 16, 32, 64]
 MAX_SLOTS = 4
 DEFAULT_READBACK_K = 1
 MAX_BLOCKS = 64
+MAX_FOLDED_PROMPT = 8  # longest prompt the graph can prefill
 
 
 def batch_buckets(max_slots: int) -> List[int]:
@@ -57,6 +62,8 @@ class SlotInfo:
         self.reused = False
         self.pending_tokens: List[int] = []
         self.last_readback_trace: List[Dict[str, int]] = []
+        self.skip_steps = 0  # folded prefill: steps whose outputs are prompt positions
+        self.drop_tokens = 0  # ring entries still to drop at readback
 
 
 class PagedDecodeState:
@@ -79,6 +86,8 @@ class PagedDecodeState:
         self.ctx_lens = torch.zeros(S, dtype=torch.int32, device=dev)  # attended length incl. new token; 0 = idle
         self.cross_lens = torch.zeros(S, dtype=torch.int32, device=dev)
         self.block_tables = torch.zeros((S, max_blocks), dtype=torch.int32, device=dev)
+        self.prompt_ids = torch.zeros((S, MAX_FOLDED_PROMPT), dtype=torch.long, device=dev)
+        self.prompt_lens = torch.zeros(S, dtype=torch.int32, device=dev)  # 0: prefilled outside the graph
         self.cross_kv = torch.zeros((S, L, 2, H, max_enc_len, D), dtype=self.dtype, device=dev)
         self.buckets = batch_buckets(S)
         self.paged_ws = {n: ops.paged_attn_workspace(n, H, D, max_blocks, dev) for n in self.buckets}
@@ -90,20 +99,34 @@ class PagedDecodeState:
                 return b
         return self.buckets[-1]
 
-    def upload_slot(self, slot: int, token: int, ctx_len: int, cross_len: int, table: Sequence[int]) -> None:
-        """Stream-ordered, non-blocking writes of one slot's row from pinned host memory."""
-        row = torch.zeros(self.max_blocks, dtype=torch.int32)
+    def upload_slot(self, slot: int, token: int, ctx_len: int, cross_len: int, table: Sequence[int],
+                    prompt: Optional[Sequence[int]] = None) -> None:
+        """Stream-ordered, non-blocking writes of one slot's row from pinned host memory.
+        With ``prompt`` the slot starts at position 0 on prompt[0] (folded prefill)."""
         if len(table) > self.max_blocks:
             raise RuntimeError(f"block table of {len(table)} blocks exceeds max_blocks={self.max_blocks}")
+        i32 = torch.zeros(self.max_blocks + 3, dtype=torch.int32)
         if table:
-            row[: len(table)] = torch.tensor(list(table), dtype=torch.int32)
-        scal = torch.tensor([ctx_len, cross_len], dtype=torch.int32)
-        tok = torch.tensor([token], dtype=torch.long)
-        row, scal, tok = row.pin_memory(), scal.pin_memory(), tok.pin_memory()
-        self.block_tables[slot].copy_(row, non_blocking=True)
-        self.ctx_lens[slot : slot + 1].copy_(scal[:1], non_blocking=True)
-        self.cross_lens[slot : slot + 1].copy_(scal[1:], non_blocking=True)
-        self.token_ids[slot : slot + 1].copy_(tok, non_blocking=True)
+            i32[: len(table)] = torch.tensor(list(table), dtype=torch.int32)
+        i64 = torch.zeros(1 + MAX_FOLDED_PROMPT, dtype=torch.long)
+        if prompt is not None:
+            if not 1 <= len(prompt) <= MAX_FOLDED_PROMPT:
+                raise ValueError(f"folded prompts hold 1..{MAX_FOLDED_PROMPT} tokens, got {len(prompt)}")
+            i64[0] = int(prompt[0])
+            i64[1 : 1 + len(prompt)] = torch.tensor(list(prompt), dtype=torch.long)
+            i32[self.max_blocks :] = torch.tensor([1, cross_len, len(prompt)], dtype=torch.int32)
+        else:
+            i64[0] = int(token)
+            i32[self.max_blocks :] = torch.tensor([ctx_len, cross_len, 0], dtype=torch.int32)
+        i32, i64 = i32.pin_memory(), i64.pin_memory()
+        mb = self.max_blocks
+        self.block_tables[slot].copy_(i32[:mb], non_blocking=True)
+        self.ctx_lens[slot : slot + 1].copy_(i32[mb : mb + 1], non_blocking=True)
+        self.cross_lens[slot : slot + 1].copy_(i32[mb + 1 : mb + 2], non_blocking=True)
+        self.prompt_lens[slot : slot + 1].copy_(i32[mb + 2 : mb + 3], non_blocking=True)
+        self.token_ids[slot : slot + 1].copy_(i64[:1], non_blocking=True)
+        if prompt is not None:
+            self.prompt_ids[slot].copy_(i64[1:], non_blocking=True)
 
     def set_table(self, slot: int, table: Sequence[int]) -> None:
         row = torch.zeros(self.max_blocks, dtype=torch.int32)
@@ -113,13 +136,17 @@ class PagedDecodeState:
     def deactivate(self, slot: int) -> None:
         self.ctx_lens[slot].zero_()
         self.cross_lens[slot].zero_()
+        self.prompt_lens[slot].zero_()
 
     def forward_step(self, n: int) -> None:
-        """One decode step over slots [0, n); graph-capturable."""
+        """One decode step over slots [0, n); graph-capturable.  A slot whose next
+        position is still inside its folded prompt is fed that prompt token."""
         nxt = self.model.decode_step_paged(self, n)
         self.next_tokens[:n].copy_(nxt)
-        self.token_ids[:n].copy_(nxt)
-        self.ctx_lens[:n] += (self.ctx_lens[:n] > 0).to(torch.int32)
+        pos = self.ctx_lens[:n]  # position of the token fed next
+        forced = self.prompt_ids[:n].gather(1, pos.clamp(max=MAX_FOLDED_PROMPT - 1).long()[:, None])[:, 0]
+        self.token_ids[:n].copy_(torch.where(pos < self.prompt_lens[:n], forced, nxt))
+        self.ctx_lens[:n] += (pos > 0).to(torch.int32)
 
 
 class GraphDecodeBuffers(PagedDecodeState):
@@ -181,12 +208,13 @@ class GraphDecodeBuffers(PagedDecodeState):
         return idx
 
     def assign_slot(self, req: Any, enc_kv_layers: Optional[List[Tuple[torch.Tensor, torch.Tensor]]], prompt_len: int,
-                    initial_tok: int, initial_self_kv: Any = None, slot_idx: Optional[int] = None,
-                    enc_seq_len: Optional[int] = None) -> int:
-        """Activates a slot for a request whose prompt K/V is already in its decoder blocks.
-        Cross K/V come from ``enc_kv_layers`` (copied in) unless the caller already wrote
-        them into ``cross_kv[slot]`` (block gather or projection GEMM) and passes
-        ``enc_seq_len``."""
+                    initial_tok: Optional[int], initial_self_kv: Any = None, slot_idx: Optional[int] = None,
+                    enc_seq_len: Optional[int] = None, fold_prompt: Optional[Sequence[int]] = None) -> int:
+        """Activates a slot.  Either the prompt K/V is already in the request's decoder
+        blocks and ``initial_tok`` is its first token, or ``fold_prompt`` holds the prompt
+        and the graph prefills it.  Cross K/V come from ``enc_kv_layers`` (copied in)
+        unless the caller already wrote them into ``cross_kv[slot]`` (block gather or
+        projection GEMM) and passes ``enc_seq_len``."""
         if slot_idx is None:
             slot_idx = self.reserve_slot()
         s = self.slots[slot_idx]
@@ -194,22 +222,28 @@ class GraphDecodeBuffers(PagedDecodeState):
             enc_seq_len = self.model.cross_kv_from_encoder(enc_kv_layers, self.cross_kv, slot_idx)
         T = min(int(enc_seq_len or self.max_enc_len), self.max_enc_len)
         s.active, s.req = True, req
-        s.decoder_seq_len = prompt_len
-        s.last_token_id = initial_tok
-        s.generated_count = 1
         s.max_new_tokens = req.max_new_tokens
         s.eos_token_id = req.eos_token_id
         s.enc_seq_len = T
-        s.pending_tokens = [initial_tok]
         s.readback_start = self._step_in_k
         s.last_readback_trace = []
-        self.upload_slot(slot_idx, initial_tok, prompt_len + 1, T, req.decoder_block_table)
+        if fold_prompt is not None:
+            s.decoder_seq_len, s.last_token_id, s.generated_count = 0, int(fold_prompt[-1]), 0
+            s.pending_tokens = []
+            s.skip_steps = s.drop_tokens = len(fold_prompt) - 1
+            self.upload_slot(slot_idx, 0, 1, T, req.decoder_block_table, prompt=fold_prompt)
+        else:
+            s.decoder_seq_len, s.last_token_id, s.generated_count = prompt_len, initial_tok, 1
+            s.pending_tokens = [initial_tok]
+            s.skip_steps = s.drop_tokens = 0
+            self.upload_slot(slot_idx, initial_tok, prompt_len + 1, T, req.decoder_block_table)
         return slot_idx
 
     def release_slot(self, slot_idx: int) -> None:
         s = self.slots[slot_idx]
         s.active, s.req = False, None
         s.pending_tokens, s.readback_start, s.last_readback_trace = [], 0, []
+        s.skip_steps = s.drop_tokens = 0
         self.deactivate(slot_idx)
         if self.zero_slot_buffers_on_release:
             self.cross_kv[slot_idx].zero_()
@@ -261,7 +295,10 @@ class GraphDecodeBuffers(PagedDecodeState):
         for s in self.slots:
             if s.active and s.req is not None:
                 s.decoder_seq_len += 1
-                s.generated_count += 1
+                if s.skip_steps > 0:
+                    s.skip_steps -= 1
+                else:
+                    s.generated_count += 1
 
     def should_readback(self) -> bool:
         if self._step_in_k >= self.readback_k:
@@ -275,9 +312,11 @@ class GraphDecodeBuffers(PagedDecodeState):
         results = []
         for i, s in enumerate(self.slots):
             if s.active and s.req is not None:
-                toks = [ring[k][i] for k in range(s.readback_start, self._step_in_k)]
+                first = min(self._step_in_k, s.readback_start + s.drop_tokens)
+                s.drop_tokens -= first - s.readback_start
+                toks = [ring[k][i] for k in range(first, self._step_in_k)]
                 s.last_readback_trace = [{"bucket": self._window_buckets[k], "readback_position": k}
-                                         for k in range(s.readback_start, self._step_in_k)]
+                                         for k in range(first, self._step_in_k)]
                 if toks:
                     s.last_token_id = toks[-1]
                     s.pending_tokens.extend(toks)

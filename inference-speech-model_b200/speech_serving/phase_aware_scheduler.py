@@ -26,6 +26,10 @@ What runs underneath is new:
 * A full-input encoder-cache hit (:492-530) skips the encoder and then runs the same
   handoff from the cached blocks, so the request is prefilled and decoded like a miss.
 * Prompt K/V from the prefill are written into the decoder blocks by op 3 (:672-690).
+  In graph mode (``graph_fold_prefill``, default on) prompts of up to eight tokens are
+  not prefilled at handoff at all: the slot starts at position 0 and the decode graph
+  feeds the prompt tokens, writing their K/V with the fused append; the first token then
+  arrives with a readback like every other token.
 """
 from __future__ import annotations
 
@@ -41,7 +45,7 @@ import torch
 
 from . import ops
 from .dual_cache_manager import DualCacheManager
-from .graph_decode_buffers import DEFAULT_READBACK_K, MAX_BLOCKS, GraphDecodeBuffers
+from .graph_decode_buffers import DEFAULT_READBACK_K, MAX_BLOCKS, MAX_FOLDED_PROMPT, GraphDecodeBuffers
 from .memory_guard import MemoryGuard
 from .phase_timing import PhaseTimer
 
@@ -126,6 +130,7 @@ class PhaseAwareSpeechScheduler:
         phase_timing: bool = False,
         max_enc_len: int = 1500,
         max_blocks: int = MAX_BLOCKS,
+        graph_fold_prefill: bool = True,
     ):
         self.model = model
         self.dual_cache = dual_cache_manager
@@ -152,6 +157,8 @@ class PhaseAwareSpeechScheduler:
                                   zero_slot_buffers_on_release=graph_zero_slot_buffers_on_release,
                                   force_bucket=graph_force_bucket)
         self.max_enc_len, self.max_blocks = max_enc_len, max_blocks
+        # graph mode: prompts of up to MAX_FOLDED_PROMPT tokens are prefilled by the decode graph
+        self.graph_fold_prefill = bool(graph_fold_prefill) and self.graph_decode
         self._buffers: Optional[GraphDecodeBuffers] = None
 
         self.queue: List[DualCacheRequest] = []
@@ -432,6 +439,13 @@ class PhaseAwareSpeechScheduler:
             for _ in range(n_blocks):
                 req.decoder_block_table.append(self.dual_cache.allocate_decoder_block())
 
+        if self.graph_fold_prefill and P <= MAX_FOLDED_PROMPT:
+            # the decode graph prefills the prompt; the first token arrives with a readback
+            buf.assign_slot(req, None, P, None, slot_idx=slot, enc_seq_len=T,
+                            fold_prompt=req.prompt_token_ids[0].tolist())
+            self.active_decode.append(req)
+            return
+
         # prefill (multi-token), then its K/V into the decoder blocks (op 3, prompt form)
         with self.phase_timer.measure([req], "prefill"), torch.no_grad():
             out = self.model.decode_step(input_ids=req.prompt_token_ids, encoder_past_kv_list=req.cached_encoder_kv,
@@ -489,6 +503,8 @@ class PhaseAwareSpeechScheduler:
                 req.last_token_id = tok
                 req.generated_tokens.append(tok)
                 req.generated_count = len(req.generated_tokens)
+                if req.first_token_time is None:
+                    req.first_token_time = time.perf_counter()
                 # graph mode counts the last token as cached (reference :753); eager mode
                 # counts the tokens whose K/V are in the pool (reference :1022)
                 req.decoder_seq_len = req.prompt_token_ids.shape[1] + req.generated_count - \
@@ -498,8 +514,9 @@ class PhaseAwareSpeechScheduler:
                     req.graph_extra_slot_steps = len(toks) - off - 1
                     if self.phase_timing:
                         self.phase_timer.ensure(req)["slot_hold_steps_after_eos"] = req.graph_extra_slot_steps
-                    if is_eos and self.graph_decode:
-                        # graph mode drops EOS and everything after it (reference :759-761)
+                    if is_eos and self.graph_decode and req.generated_count > 1:
+                        # graph mode drops EOS and everything after it (reference :759-761); an
+                        # EOS first token is kept, as when the prefill produced it (:696-700)
                         req.generated_tokens = req.generated_tokens[: req.generated_tokens.index(tok)]
                     self._complete_request(req, status=RequestPhase.COMPLETED)
                     done.append(req)

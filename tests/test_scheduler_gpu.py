@@ -242,3 +242,24 @@ def test_pretrained_whisper_tokens_follow_hf_decoder(dtype, graph):
             margin = float(row.max() - row[t])
             assert margin <= tol + 1e-4 * float(row.abs().max()), (i, t, int(row.argmax()), margin)
     assert enc.allocated_block_count == 0 and dec.allocated_block_count == 0
+
+
+@pytest.mark.parametrize("readback", [1, 4])
+def test_graph_folded_prefill_matches_handoff_prefill(readback):
+    """Prompts prefilled by the decode graph (fused K/V append per prompt token) give the
+    same tokens as the multi-token prefill at handoff (fp32, 4-token Whisper prompt)."""
+    torch.manual_seed(11)
+    model = WhisperClassSpeechEncoderDecoderModel(2, 2, 4, 64, 80, 51865).to(DEV).eval()
+    mels = [torch.randn(80, n, device=DEV) for n in (120, 300, 64)]
+    toks = {}
+    for fold in (False, True):
+        s, enc, dec = _sched(model, 128, 128, bs=8, dtype=torch.float32, graph_decode=True,
+                             graph_readback_k=readback, graph_fold_prefill=fold, eos_token_id=-1)
+        for m in mels:
+            s.submit(m, max_new_tokens=9, eos_token_id=-1)
+        done = sorted(s.run_until_done(), key=lambda r: r.id)
+        toks[fold] = [r.generated_tokens for r in done]
+        assert all(len(t) == 9 for t in toks[fold])
+        assert all(r.first_token_time is not None for r in done)
+        assert dec.allocated_block_count == 0 and s.graph_buffers.active_slot_count() == 0
+    assert toks[True] == toks[False]
