@@ -30,10 +30,11 @@
 //   compute warps: it patches its own slice of an appended row; at the end of an item it
 //   writes the output (an item covering the whole sequence) or a partial (m, l, acc) to
 //   slot [item][h].
-// * Split sequences are merged by a second, small kernel (one warp per (sequence, head),
-//   item-parallel loads) launched with programmatic dependent launch: the streaming
-//   kernel signals launch_dependents at its start, so the merge kernel's CTAs are already
-//   resident and waiting (griddepcontrol.wait) when the streaming kernel ends.
+// * Split sequences are merged by a second, small kernel (one warp per (sequence, head))
+//   launched with programmatic dependent launch: the streaming kernel signals
+//   launch_dependents at its start, so the merge kernel's CTAs are already resident, have
+//   located their items, and wait (griddepcontrol.wait) when the streaming kernel ends;
+//   then one round of loads brings in every partial of the sequence.
 // * q·k: 32/block_size lanes per row, q (pre-scaled by scale*log2 e) in registers, K
 //   chunks read in a per-row rotated order so the 8 lanes of a shared-memory phase hit
 //   distinct banks.  p·v: each lane owns one 16-byte chunk of a row.  Online softmax in
@@ -484,68 +485,87 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
 }
 
 // ------------------------------------------------------------------ merge kernel
-// One warp per (sequence, head) of a sequence that spans more than one item: reads the
-// items' partial (m, l, acc) in parallel (lane = item for m and l; all items' acc loads
-// issued before any is used) and writes acc_total / l_total.
+// One warp per (sequence, head) of a sequence that spans more than one item.  Launched
+// with programmatic dependent launch right behind the streaming kernel.  The lengths are
+// read, and the sequence's item range worked out, while the streaming kernel still runs:
+// the streaming kernel never writes them, and it triggers this launch only after its own
+// griddepcontrol.wait, so everything written before it is final.  After
+// griddepcontrol.wait every partial of the sequence is loaded in one round trip (lane =
+// item for (m, l); all items' acc before any of it is used).
 template <typename T, int D, int BS>
 __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // the streaming kernel has finished
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  constexpr int DL = (D + 31) / 32;  // acc elements per lane
+  constexpr int MAXI = 32;           // items per sequence held in registers
   const int lane = threadIdx.x & 31;
   const long long pair = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  if (pair >= (long long)p.B * p.H) return;
-  const int b = (int)(pair / p.H), h = (int)(pair % p.H);
+  const bool live = pair < (long long)p.B * p.H;
+  const int b = live ? (int)(pair / p.H) : 0, h = live ? (int)(pair % p.H) : 0;
   const int max_ctx = p.max_blocks * BS;
-  int i0 = 0, ctx_b = 0;
-  // item index of sequence b's first item = sum over b' < b of ceil(ceil(ctx/BS)/kItemUnits)
-  for (int bb = lane; bb <= b; bb += 32) {
+  // sequence b's first item = sum over b' < b of ceil(ceil(ctx/BS)/kItemUnits)
+  int ctx_b = live ? p.context_lens[b] : 0;
+  ctx_b = ctx_b > max_ctx ? max_ctx : (ctx_b > 0 ? ctx_b : 0);
+  int i0 = 0;
+  for (int bb = lane; bb < b && live; bb += 32) {
     int c = p.context_lens[bb];
     c = c > max_ctx ? max_ctx : (c > 0 ? c : 0);
-    const int n = ((c + BS - 1) / BS + kItemUnits - 1) / kItemUnits;
-    if (bb < b) i0 += n;
-    else ctx_b = c;
+    i0 += ((c + BS - 1) / BS + kItemUnits - 1) / kItemUnits;
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    i0 += __shfl_xor_sync(0xffffffffu, i0, o);
-    ctx_b = max(ctx_b, __shfl_xor_sync(0xffffffffu, ctx_b, o));
-  }
+  for (int o = 16; o > 0; o >>= 1) i0 += __shfl_xor_sync(0xffffffffu, i0, o);
   const int nitems = ((ctx_b + BS - 1) / BS + kItemUnits - 1) / kItemUnits;
-  if (nitems <= 1) return;  // written by the streaming kernel (or zero)
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the streaming kernel has finished
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (!live || nitems <= 1) return;  // written by the streaming kernel (or zero)
   const float* base = p.partials + ((size_t)i0 * p.H + h) * (D + 2);
   const size_t stride = (size_t)p.H * (D + 2);  // next item, same head
+  T* orow = reinterpret_cast<T*>(p.out) + ((size_t)b * p.H + h) * D;
+  if (nitems <= MAXI) {
+    float2 ml = make_float2(-INFINITY, 0.f);
+    float a[MAXI][DL];
+    if (lane < nitems) ml = __ldcg(reinterpret_cast<const float2*>(base + lane * stride + D));
+#pragma unroll
+    for (int it = 0; it < MAXI; ++it) {
+#pragma unroll
+      for (int e = 0; e < DL; ++e) {
+        const int d = lane + 32 * e;
+        a[it][e] = (it < nitems && d < D) ? __ldcg(base + it * stride + d) : 0.f;
+      }
+    }
+    const float M = warp_max(ml.x);
+    const float w = lane < nitems ? exp2f(ml.x - M) : 0.f;
+    const float inv = 1.f / warp_sum(ml.y * w);
+    float o[DL];
+#pragma unroll
+    for (int e = 0; e < DL; ++e) o[e] = 0.f;
+#pragma unroll
+    for (int it = 0; it < MAXI; ++it) {
+      const float wi = __shfl_sync(0xffffffffu, w, it);
+#pragma unroll
+      for (int e = 0; e < DL; ++e) o[e] = fmaf(wi, a[it][e], o[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < DL; ++e) {
+      const int d = lane + 32 * e;
+      if (d < D) orow[d] = Elem<T>::from_f(o[e] * inv);
+    }
+    return;
+  }
+  // long sequences: two passes over the items
   float M = -INFINITY;
   for (int it = lane; it < nitems; it += 32) M = fmaxf(M, __ldcg(base + it * stride + D));
   M = warp_max(M);
   float L = 0.f;
-  for (int it = lane; it < nitems; it += 32) L += __ldcg(base + it * stride + D + 1) * exp2f(__ldcg(base + it * stride + D) - M);
-  L = warp_sum(L);
-  const float inv = 1.f / L;
-  T* orow = reinterpret_cast<T*>(p.out) + ((size_t)b * p.H + h) * D;
-  for (int d0 = 2 * lane; d0 < D; d0 += 64) {
-    float2 o = make_float2(0.f, 0.f);
-    constexpr int U = 8;
-    for (int it0 = 0; it0 < nitems; it0 += U) {
-      float2 v[U];
-      float w[U];
+  for (int it = lane; it < nitems; it += 32)
+    L += __ldcg(base + it * stride + D + 1) * exp2f(__ldcg(base + it * stride + D) - M);
+  const float inv = 1.f / warp_sum(L);
 #pragma unroll
-      for (int u = 0; u < U; ++u) {  // issue every load of this batch before using any
-        const int it = it0 + u;
-        if (it < nitems) {
-          v[u] = __ldcg(reinterpret_cast<const float2*>(base + it * stride + d0));
-          w[u] = __ldcg(base + it * stride + D);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        if (it0 + u < nitems) {
-          const float ww = exp2f(w[u] - M);
-          o = __ffma2_rn(v[u], make_float2(ww, ww), o);
-        }
-      }
-    }
-    orow[d0] = Elem<T>::from_f(o.x * inv);
-    if (d0 + 1 < D) orow[d0 + 1] = Elem<T>::from_f(o.y * inv);
+  for (int e = 0; e < DL; ++e) {
+    const int d = lane + 32 * e;
+    if (d >= D) break;
+    float o = 0.f;
+    for (int it = 0; it < nitems; ++it)
+      o = fmaf(exp2f(__ldcg(base + it * stride + D) - M), __ldcg(base + it * stride + d), o);
+    orow[d] = Elem<T>::from_f(o * inv);
   }
 }
 

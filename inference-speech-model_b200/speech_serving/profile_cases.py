@@ -6,7 +6,8 @@
     python -m speech_serving.profile_cases cross_cfg3 --time 50   # CUDA-event timing
 
 Cases: paged_cfg2 = paged self-attention B=64 H=12 D=64 bs=16
-ctx~U[1,448] fp16; cross_cfg3 = cross-attention B=128 H=20 D=64 T=1500 valid~U[300,1500]
+ctx~U[1,448] fp16 (paged_big: the same with B=512 and every context 448, a launch long
+enough that set-up and tail are small); cross_cfg3 = cross-attention B=128 H=20 D=64 T=1500 valid~U[300,1500]
 bf16; proj_small / proj_large = the handoff cross-KV projection of one 1500-position
 request for Whisper-small (d 768, 12 layers x 12 heads) / large-v3 (d 1280, 32 x 20), bf16.
 Each launch reads a different input set so that DRAM counters see cold data.
@@ -23,19 +24,19 @@ from . import ops
 WORK = {}  # case -> (algorithmic bytes or flops per launch, unit)
 
 
-def _paged(dev, sets):
+def _paged(dev, sets, B=64, NB=4096, lo=1, name="paged_cfg2"):
     g = torch.Generator().manual_seed(0)
-    B, H, D, bs, NB = 64, 12, 64, 16, 4096
+    H, D, bs = 12, 64, 16
     out = []
     for i in range(sets):
-        ctx = torch.randint(1, 449, (B,), generator=g, dtype=torch.int32)
+        ctx = torch.randint(lo, 449, (B,), generator=g, dtype=torch.int32)
         tables = torch.randperm(NB, generator=g)[: B * 28].view(B, 28).to(torch.int32)
         q = torch.randn(B, H, D, device=dev).half()
         kp = torch.randn(NB, bs, H, D, device=dev).half()
         vp = torch.randn(NB, bs, H, D, device=dev).half()
         out.append((q, kp, vp, tables.to(dev), ctx.to(dev)))
     ws = ops.paged_attn_workspace(B, H, D, 28, dev)
-    WORK["paged_cfg2"] = (sum(int(o[4].sum()) * H * D * 4 + 2 * B * H * D * 2 for o in out) / sets, "GB/s")
+    WORK[name] = (sum(int(o[4].sum()) * H * D * 4 + 2 * B * H * D * 2 for o in out) / sets, "GB/s")
     return lambda i: ops.paged_decode_attention(*out[i % sets], scale=0.125, workspace=ws)
 
 
@@ -64,6 +65,7 @@ def _proj(dev, sets, d, L, H):
 
 CASES = {
     "paged_cfg2": lambda dev, n: _paged(dev, n),
+    "paged_big": lambda dev, n: _paged(dev, n, B=512, NB=16384, lo=448, name="paged_big"),
     "cross_cfg3": lambda dev, n: _cross(dev, n),
     "proj_small": lambda dev, n: _proj(dev, n, 768, 12, 12),
     "proj_large": lambda dev, n: _proj(dev, n, 1280, 32, 20),
