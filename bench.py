@@ -363,41 +363,71 @@ def run_ours(args):
     achieved = (bytes_rank / args.steps) / (launch_ms / 1e3) / 1e9
 
     # ---- e2e through the public API with pinned host buffers ----------------------
+    # Every step copies its q, block tables and lengths from pinned host memory and its
+    # output back.  The K steps' public-API calls are captured in one CUDA graph; the
+    # copies run on two copy streams into double-buffered device inputs, so step i+1's
+    # inputs (and step i-1's output) move while step i's kernel runs.
     hq = [s["q"].cpu().pin_memory() for s in sets]
     ht = [s["tables"].cpu().pin_memory() for s in sets]
     hc = [s["ctx"].cpu().pin_memory() for s in sets]
     hout = [torch.empty(c["B"], c["H"], c["D"], dtype=torch.float16).pin_memory() for _ in range(N_SETS)]
-    dq = torch.empty_like(sets[0]["q"])
-    dt_ = torch.empty_like(sets[0]["tables"])
-    dc = torch.empty_like(sets[0]["ctx"])
-    dout = torch.empty_like(outs[0])
+    dq = [torch.empty_like(sets[0]["q"]) for _ in range(2)]
+    dt_ = [torch.empty_like(sets[0]["tables"]) for _ in range(2)]
+    dc = [torch.empty_like(sets[0]["ctx"]) for _ in range(2)]
+    dout = [torch.empty_like(outs[0]) for _ in range(2)]
+    s_h2d, s_d2h = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    K = args.steps
+    h2d_done = [torch.cuda.Event() for _ in range(K)]
+    k_done = [torch.cuda.Event() for _ in range(K)]
+    d2h_done = [torch.cuda.Event() for _ in range(K)]
 
-    def e2e_step(i):
-        j = i % N_SETS
-        dq.copy_(hq[j], non_blocking=True)
-        dt_.copy_(ht[j], non_blocking=True)
-        dc.copy_(hc[j], non_blocking=True)
-        ops.paged_decode_attention(dq, sets[j]["k_pool"], sets[j]["v_pool"], dt_, dc, scale=c["scale"], out=dout,
-                                   workspace=ws)
-        hout[j].copy_(dout, non_blocking=True)
+    def e2e_steps():
+        main = torch.cuda.current_stream()
+        s_h2d.wait_stream(main)
+        s_d2h.wait_stream(main)
+        for i in range(K):
+            b, j = i % 2, i % N_SETS
+            with torch.cuda.stream(s_h2d):
+                if i >= 2:
+                    s_h2d.wait_event(k_done[i - 2])  # buffer b was read by step i-2
+                dq[b].copy_(hq[j], non_blocking=True)
+                dt_[b].copy_(ht[j], non_blocking=True)
+                dc[b].copy_(hc[j], non_blocking=True)
+                h2d_done[i].record(s_h2d)
+            main.wait_event(h2d_done[i])
+            if i >= 2:
+                main.wait_event(d2h_done[i - 2])  # output buffer b was read back
+            ops.paged_decode_attention(dq[b], sets[j]["k_pool"], sets[j]["v_pool"], dt_[b], dc[b], scale=c["scale"],
+                                       out=dout[b], workspace=ws)
+            k_done[i].record(main)
+            with torch.cuda.stream(s_d2h):
+                s_d2h.wait_event(k_done[i])
+                hout[j].copy_(dout[b], non_blocking=True)
+                d2h_done[i].record(s_d2h)
+        main.wait_stream(s_h2d)
+        main.wait_stream(s_d2h)
 
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph, stream=stream):
+        e2e_steps()
     with torch.cuda.stream(stream):
-        for i in range(3):
-            e2e_step(i)
+        e2e_graph.replay()  # warm
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record(stream)
-        for i in range(args.steps):
-            e2e_step(i)
+        e2e_graph.replay()
         e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms_max = replicas.max_over_ranks(e0.elapsed_time(e1))
     e2e_value = replicas.whole_job_rate(replicas.sum_over_ranks(bytes_rank), e2e_ms_max) / 1e9
-    h2d = dq.numel() * 2 + dt_.numel() * 4 + dc.numel() * 4
-    d2h = dout.numel() * 2
+    h2d = dq[0].numel() * 2 + dt_[0].numel() * 4 + dc[0].numel() * 4
+    d2h = dout[0].numel() * 2
+    # the read-back outputs are the kernel's: last rotation of host buffers vs the oracle below
+    e2e_out_last = hout[(K - 1) % N_SETS].clone()
+    del e2e_graph
 
     # correctness guard on the timed data: one set against the oracle's C port
     ok_err = None
@@ -413,6 +443,12 @@ def run_ours(args):
         ops.paged_decode_attention(s0["q"], s0["k_pool"], s0["v_pool"], s0["tables"], s0["ctx"], scale=c["scale"],
                                    out=outs[0], workspace=ws)
         ok_err = float(np.abs(outs[0].float().cpu().numpy() - ref).max())
+        jl = (args.steps - 1) % N_SETS  # the e2e leg's read-back outputs are the kernel's
+        sl = sets[jl]
+        chk = ops.paged_decode_attention(sl["q"], sl["k_pool"], sl["v_pool"], sl["tables"], sl["ctx"], scale=c["scale"],
+                                         workspace=ws)
+        if not torch.equal(chk.cpu(), e2e_out_last):
+            raise RuntimeError("e2e read-back differs from the device-resident call on the same inputs")
         if ok_err > 2e-3:
             raise RuntimeError(f"benchmark output differs from the oracle by {ok_err}")
         if ops.read_error_word(ws) != 0:
@@ -462,7 +498,9 @@ def run_ours(args):
                      "peak_source": f"{peak_kind} hbm_gbs (copy bandwidth)",
                      "bytes_per_launch": int(bytes_rank / args.steps), "launch_us": round(launch_ms * 1e3, 3)},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "path": "speech_serving.ops.paged_decode_attention (ctypes -> C ABI), pinned host buffers"},
+                "path": "speech_serving.ops.paged_decode_attention (ctypes -> C ABI), pinned host buffers; the K steps "
+                        "captured in one CUDA graph, copies on two copy streams overlapping the previous step's kernel "
+                        "(double-buffered device inputs)"},
         "gpu_launches": 2 * args.steps,  # streaming kernel + split merge kernel per step
         "clocks": sampler.summary(),
         "max_abs_err_vs_oracle": ok_err,
