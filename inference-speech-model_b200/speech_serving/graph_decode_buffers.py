@@ -88,7 +88,10 @@ class PagedDecodeState:
         self.block_tables = torch.zeros((S, max_blocks), dtype=torch.int32, device=dev)
         self.prompt_ids = torch.zeros((S, MAX_FOLDED_PROMPT), dtype=torch.long, device=dev)
         self.prompt_lens = torch.zeros(S, dtype=torch.int32, device=dev)  # 0: prefilled outside the graph
-        self.cross_kv = torch.zeros((S, L, 2, H, max_enc_len, D), dtype=self.dtype, device=dev)
+        # S slots plus one spare that batched encoder graphs write their padding rows into
+        self.cross_kv_all = torch.zeros((S + 1, L, 2, H, max_enc_len, D), dtype=self.dtype, device=dev)
+        self.cross_kv = self.cross_kv_all[:S]
+        self.spare_slot = S
         self.buckets = batch_buckets(S)
         self.paged_ws = {n: ops.paged_attn_workspace(n, H, D, max_blocks, dev) for n in self.buckets}
         self.cross_ws = {n: ops.cross_attn_workspace(n, H, D, dev) for n in self.buckets}
@@ -328,6 +331,6 @@ class GraphDecodeBuffers(PagedDecodeState):
 
     def vram_overhead_mb(self) -> float:
         """Slot buffers owned here (the self-K/V lives in the BlockManager's pool)."""
-        b = self.cross_kv.numel() * self.cross_kv.element_size() + self.block_tables.numel() * 4
+        b = self.cross_kv_all.numel() * self.cross_kv_all.element_size() + self.block_tables.numel() * 4
         b += sum(w.numel() for w in self.paged_ws.values()) + sum(w.numel() for w in self.cross_ws.values())
         return b / 1024 ** 2

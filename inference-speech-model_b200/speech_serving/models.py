@@ -317,6 +317,67 @@ class PretrainedWhisperModel(nn.Module):
             slots[slot, l, 1, :, :T].copy_(v[0])
         return T
 
+    # ---- encoder + projection as CUDA graphs, one per batch bucket ----------------------
+    def encode_into_slots(self, mel_features: torch.Tensor, out_slots: torch.Tensor, slots: Sequence[int],
+                          spare_slot: int, buckets: Sequence[int], use_graphs: bool = True) -> torch.Tensor:
+        """Encoder forward and the op-4 projection of a batch straight into graph slots
+        ``slots`` of ``out_slots`` ([S, L, 2, H, T_out, D]).  With 16-bit weights and
+        full-length inputs (2 * max_source_positions frames) the pair runs as a CUDA graph
+        captured per batch bucket (the batch is padded to the bucket; padding rows project
+        into ``spare_slot``, which decoding never reads), so a batch costs one replay
+        instead of one launch per encoder op.  Returns the encoder output [B, T, d]."""
+        n = mel_features.shape[0]
+        frames = 2 * self.config.max_source_positions
+        graphable = (use_graphs and self.dtype in (torch.float16, torch.bfloat16) and mel_features.shape[-1] == frames
+                     and n <= max(buckets) and str(out_slots.device).startswith("cuda"))
+        dev = out_slots.device
+        if not graphable:
+            ids = torch.tensor(list(slots), dtype=torch.int32).to(dev, non_blocking=True)
+            enc, _ = self.encode(mel_features, out_slots=out_slots, slot_ids=ids)
+            return enc
+        bucket = min(b for b in buckets if b >= n)
+        graphs = self.__dict__.setdefault("_enc_graphs", {})
+        key = (bucket, out_slots.data_ptr())
+        if key not in graphs:
+            self._capture_encoder_graphs(out_slots, spare_slot, buckets)
+        g, mel_buf, ids_buf, hidden = graphs[key]
+        mel_buf[:n].copy_(mel_features, non_blocking=True)
+        ids = torch.full((bucket,), spare_slot, dtype=torch.int32)
+        ids[:n] = torch.tensor(list(slots), dtype=torch.int32)
+        ids_buf.copy_(ids.pin_memory(), non_blocking=True)
+        g.replay()
+        return hidden[:n]
+
+    def _capture_encoder_graphs(self, out_slots: torch.Tensor, spare_slot: int, buckets: Sequence[int]) -> None:
+        """Captures encoder + projection for every bucket at once (they share one memory
+        pool and are replayed one at a time)."""
+        graphs = self.__dict__.setdefault("_enc_graphs", {})
+        dev = out_slots.device
+        frames = 2 * self.config.max_source_positions
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        pool = self.__dict__.get("_enc_pool")
+        for bucket in sorted(buckets):
+            key = (bucket, out_slots.data_ptr())
+            if key in graphs:
+                continue
+            mel_buf = torch.zeros((bucket, self.config.num_mel_bins, frames), dtype=self.dtype, device=dev)
+            ids_buf = torch.full((bucket,), spare_slot, dtype=torch.int32, device=dev)
+            with torch.cuda.stream(side), torch.no_grad():
+                for _ in range(2):
+                    self.encode(mel_buf, out_slots=out_slots, slot_ids=ids_buf)
+            side.synchronize()
+            g = torch.cuda.CUDAGraph()
+            kw = {"pool": pool} if pool is not None else {}
+            with torch.cuda.graph(g, stream=side, **kw), torch.no_grad():
+                hidden, _ = self.encode(mel_buf, out_slots=out_slots, slot_ids=ids_buf)
+            if pool is None:
+                pool = g.pool()
+                self.__dict__["_enc_pool"] = pool
+            graphs[key] = (g, mel_buf, ids_buf, hidden)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+
     def decode_step(self, input_ids, past_key_values=None, encoder_past_kv_list=None, encoder_hidden_states=None,
                     attention_mask=None, encoder_attention_mask=None, position_ids=None, use_cache=True, **kwargs):
         """Multi-token HF decoder forward (prompt prefill), cross K/V from the encoder's

@@ -102,6 +102,7 @@ class DualCacheRequest:
     first_token_time: Optional[float] = None
     finish_time: Optional[float] = None
     phase_timing: Optional[Dict[str, Any]] = None
+    enc_ready: Optional[Any] = None  # CUDA event: the encoder stream has written this request's slot
 
 
 class PhaseAwareSpeechScheduler:
@@ -131,6 +132,7 @@ class PhaseAwareSpeechScheduler:
         max_enc_len: int = 1500,
         max_blocks: int = MAX_BLOCKS,
         graph_fold_prefill: bool = True,
+        graph_encoder: bool = True,
     ):
         self.model = model
         self.dual_cache = dual_cache_manager
@@ -159,6 +161,8 @@ class PhaseAwareSpeechScheduler:
         self.max_enc_len, self.max_blocks = max_enc_len, max_blocks
         # graph mode: prompts of up to MAX_FOLDED_PROMPT tokens are prefilled by the decode graph
         self.graph_fold_prefill = bool(graph_fold_prefill) and self.graph_decode
+        # graph mode + direct handoff: encoder and projection replayed as per-bucket graphs
+        self.graph_encoder = bool(graph_encoder) and self.graph_decode
         self._buffers: Optional[GraphDecodeBuffers] = None
 
         self.queue: List[DualCacheRequest] = []
@@ -178,6 +182,11 @@ class PhaseAwareSpeechScheduler:
         self._full_input_enc_cache: Dict[str, Dict[str, Any]] = {}
         self.decode_steps = 0
         self.decode_time_s = 0.0
+        # graph mode: the encoder runs on its own stream; requests it has handed off wait
+        # here (slot reserved, blocks allocated) until their encoder event has completed,
+        # then join the decode graph at the next step
+        self._enc_stream: Optional[torch.cuda.Stream] = None
+        self._pending_activation: List[Tuple[DualCacheRequest, int, int, int, List[int]]] = []
 
     # ---- slots (created on first use, so admission logic also runs without a GPU) --------
     @property
@@ -286,7 +295,7 @@ class PhaseAwareSpeechScheduler:
 
     def _process_encode_phase(self) -> None:
         enc_bm = self.dual_cache.encoder_bm
-        free_slots = self.max_batch_size - (len(self.active_encode) + len(self.active_decode))
+        free_slots = self.max_batch_size - self._occupied()
         if self.batch_encoder and free_slots > 1 and len(self.queue) > 1 and not self.retain_encoder_cache:
             batch, need = [], 0
             while self.queue and len(batch) < free_slots:
@@ -315,7 +324,7 @@ class PhaseAwareSpeechScheduler:
             if batch:
                 self.queue.insert(0, batch[0])
 
-        while len(self.active_encode) + len(self.active_decode) < self.max_batch_size and self.queue:
+        while self._occupied() < self.max_batch_size and self.queue:
             nxt = self.queue[0]
             mel_in = nxt.mel_features.unsqueeze(0) if nxt.mel_features.dim() == 2 else nxt.mel_features
             full_hash = self._compute_full_input_hash(mel_in)
@@ -367,8 +376,28 @@ class PhaseAwareSpeechScheduler:
         written straight into it (no K/V list is returned then)."""
         if self.graph_direct_encoder_kv and getattr(self.model, "encodes_into_slots", False):
             slots = [self._reserve_slot(r) for r in reqs]
-            ids = torch.tensor(slots, dtype=torch.int32).to(self.graph_buffers.device, non_blocking=True)
-            return self.model.encode(mels, out_slots=self.graph_buffers.cross_kv, slot_ids=ids)
+            buf = self.graph_buffers
+            if hasattr(self.model, "encode_into_slots"):
+                if not self.graph_encoder:
+                    hidden = self.model.encode_into_slots(mels, buf.cross_kv_all, slots, buf.spare_slot, buf.buckets,
+                                                          use_graphs=False)
+                    return hidden, None
+                # on the encoder stream, overlapping the decode graph of the requests in flight
+                main = torch.cuda.current_stream(buf.device)
+                if self._enc_stream is None:
+                    self._enc_stream = torch.cuda.Stream(device=buf.device)
+                es = self._enc_stream
+                es.wait_stream(main)
+                mels.record_stream(es)
+                with torch.cuda.stream(es):
+                    hidden = self.model.encode_into_slots(mels, buf.cross_kv_all, slots, buf.spare_slot, buf.buckets)
+                ev = torch.cuda.Event()
+                ev.record(es)
+                for r in reqs:
+                    r.enc_ready = ev
+                return hidden, None
+            ids = torch.tensor(slots, dtype=torch.int32).to(buf.device, non_blocking=True)
+            return self.model.encode(mels, out_slots=buf.cross_kv, slot_ids=ids)
         return self.model.encode(mels)
 
     def _setup_safely(self, req, hidden, kv, full_hash, enc_time) -> None:
@@ -441,10 +470,16 @@ class PhaseAwareSpeechScheduler:
 
         if self.graph_fold_prefill and P <= MAX_FOLDED_PROMPT:
             # the decode graph prefills the prompt; the first token arrives with a readback
-            buf.assign_slot(req, None, P, None, slot_idx=slot, enc_seq_len=T,
-                            fold_prompt=req.prompt_token_ids[0].tolist())
+            prompt = req.prompt_token_ids[0].tolist()
+            if req.enc_ready is not None:  # its encoder is still running on the encoder stream
+                self._pending_activation.append((req, slot, P, T, prompt))
+                return
+            buf.assign_slot(req, None, P, None, slot_idx=slot, enc_seq_len=T, fold_prompt=prompt)
             self.active_decode.append(req)
             return
+        if req.enc_ready is not None:  # the prefill below reads the slot's cross K/V
+            torch.cuda.current_stream(buf.device).wait_event(req.enc_ready)
+            req.enc_ready = None
 
         # prefill (multi-token), then its K/V into the decoder blocks (op 3, prompt form)
         with self.phase_timer.measure([req], "prefill"), torch.no_grad():
@@ -467,7 +502,31 @@ class PhaseAwareSpeechScheduler:
         self.active_decode.append(req)
 
     # ---- decode phase --------------------------------------------------------------------------
+    def _occupied(self) -> int:
+        """Requests holding a slot: encoding, decoding, or handed off and waiting for
+        their encoder."""
+        return len(self.active_encode) + len(self.active_decode) + len(self._pending_activation)
+
+    def _activate_pending(self) -> None:
+        """Slots whose encoder has finished join the decode graph; with nothing else to
+        decode, wait for the oldest one."""
+        if not self._pending_activation:
+            return
+        buf = self.graph_buffers
+        if not self.active_decode:
+            self._pending_activation[0][0].enc_ready.synchronize()
+        keep = []
+        for req, slot, P, T, prompt in self._pending_activation:
+            if req.enc_ready.query():
+                req.enc_ready = None
+                buf.assign_slot(req, None, P, None, slot_idx=slot, enc_seq_len=T, fold_prompt=prompt)
+                self.active_decode.append(req)
+            else:
+                keep.append((req, slot, P, T, prompt))
+        self._pending_activation = keep
+
     def _process_decode_phase(self) -> None:
+        self._activate_pending()
         if not self.active_decode:
             return
         buf = self.graph_buffers
@@ -561,7 +620,7 @@ class PhaseAwareSpeechScheduler:
         self.peak_actually_used_bytes = max(self.peak_actually_used_bytes, used)
 
     def step(self) -> bool:
-        in_flight = len(self.active_encode) + len(self.active_decode)
+        in_flight = self._occupied()
         self.peak_in_flight_requests = max(self.peak_in_flight_requests, in_flight)
         self.in_flight_history.append(in_flight)
         self._update_peak_actually_used()
@@ -577,7 +636,7 @@ class PhaseAwareSpeechScheduler:
         return self.has_work()
 
     def has_work(self) -> bool:
-        return bool(self.queue or self.active_encode or self.active_decode)
+        return bool(self.queue or self.active_encode or self.active_decode or self._pending_activation)
 
     def run_until_done(self, max_steps: int = 10000) -> List[DualCacheRequest]:
         steps = 0

@@ -213,12 +213,16 @@ def _hf_model(dtype):
     return PretrainedWhisperModel(config=cfg, device=DEV, dtype=dtype, seed=0)
 
 
-@pytest.mark.parametrize("dtype,graph", [(torch.float32, False), (torch.float16, True), (torch.bfloat16, True)])
-def test_pretrained_whisper_tokens_follow_hf_decoder(dtype, graph):
+@pytest.mark.parametrize("dtype,graph,direct", [(torch.float32, False, False), (torch.float16, True, False),
+                                                (torch.bfloat16, True, False), (torch.float16, True, True),
+                                                (torch.bfloat16, True, True)])
+def test_pretrained_whisper_tokens_follow_hf_decoder(dtype, graph, direct):
     """Every generated token is the HF decoder's argmax (teacher-forced on the same
-    prefix), up to a near-tie margin in 16-bit types."""
+    prefix), up to a near-tie margin in 16-bit types.  The direct-handoff cases run the
+    encoder and the slot projection as per-bucket CUDA graphs."""
     model = _hf_model(dtype)
-    s, enc, dec = _sched(model, 64, 64, bs=16, dtype=dtype, graph_decode=graph, graph_readback_k=2)
+    s, enc, dec = _sched(model, 64, 64, bs=16, dtype=dtype, graph_decode=graph, graph_readback_k=2,
+                         graph_direct_encoder_kv=direct, batch_encoder=direct)
     torch.manual_seed(3)
     mels = [torch.randn(80, 200, device=DEV) for _ in range(3)]
     for m in mels:
