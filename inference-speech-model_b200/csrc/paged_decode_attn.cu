@@ -35,12 +35,14 @@
 //   launch_dependents at its start, so the merge kernel's CTAs are already resident, have
 //   located their items, and wait (griddepcontrol.wait) when the streaming kernel ends;
 //   then one round of loads brings in every partial of the sequence.
-// * q·k: 32/block_size lanes per row, q (pre-scaled by scale*log2 e) in registers, K
+// * q·k: 32/block_size lanes per row, q in registers (each score scaled by scale*log2 e), K
 //   chunks read in a per-row rotated order so the 8 lanes of a shared-memory phase hit
 //   distinct banks.  p·v: each lane owns one 16-byte chunk of a row.  Online softmax in
 //   base 2; packed fp32x2 FMAs.
 // * Every wait is bounded; a warp whose wait runs out records SPD_DEVERR_TIMEOUT, raises
 //   the CTA's abort flag and leaves, and the others' bounded waits then run out too.
+#include <type_traits>
+
 #include "spd_params.cuh"
 
 // Timeline hook: expands to nothing unless a tracing build defines it (to record
@@ -356,12 +358,7 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
 #pragma unroll
           for (int cc = 0; cc < NCH; ++cc) {
             const int ci = (cc + rot) & (NCH - 1);
-            load_f2<T, CH>(qrow + ci * CH, &qr[k][cc * CH / 2]);
-#pragma unroll
-            for (int e = 0; e < CH / 2; ++e) {
-              qr[k][cc * CH / 2 + e].x *= p.scale_log2;
-              qr[k][cc * CH / 2 + e].y *= p.scale_log2;
-            }
+            load_f2<T, CH>(qrow + ci * CH, &qr[k][cc * CH / 2]);  // the score is scaled instead
           }
         }
       }
@@ -392,50 +389,60 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
       __syncwarp();
     }
 
+    // One head of one block; FULL: all BS rows valid (every block but a sequence's last),
+    // compiled without the per-row checks.
+    auto head_block = [&](auto full_tag) {
+      constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll
-    for (int k = 0; k < HPW; ++k) {
-      const int h = warp * HPW + k;
-      if (h >= H) continue;
-      const T* Kh = Ks + h * D;
-      const T* Vh = Vs + h * D;
-      float sc = -INFINITY;
-      if (r < nvalid) {
-        const T* krow = Kh + (size_t)r * HD + sub * DPL;
-        float2 dot = make_float2(0.f, 0.f);
+      for (int k = 0; k < HPW; ++k) {
+        const int h = warp * HPW + k;
+        if (h >= H) continue;
+        const T* Kh = Ks + h * D;
+        const T* Vh = Vs + h * D;
+        const bool rv = FULL || r < nvalid;
+        float sc = 0.f;
+        if (rv) {
+          const T* krow = Kh + (size_t)r * HD + sub * DPL;
+          float2 dot = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int cc = 0; cc < NCH; ++cc) {
-          const int ci = (cc + rot) & (NCH - 1);
-          float2 kv[CH / 2];
-          load_f2<T, CH>(krow + ci * CH, kv);
+          for (int cc = 0; cc < NCH; ++cc) {
+            const int ci = (cc + rot) & (NCH - 1);
+            float2 kv[CH / 2];
+            load_f2<T, CH>(krow + ci * CH, kv);
 #pragma unroll
-          for (int e = 0; e < CH / 2; ++e) dot = __ffma2_rn(qr[k][cc * CH / 2 + e], kv[e], dot);
+            for (int e = 0; e < CH / 2; ++e) dot = __ffma2_rn(qr[k][cc * CH / 2 + e], kv[e], dot);
+          }
+          sc = dot.x + dot.y;
         }
-        sc = dot.x + dot.y;
-      }
 #pragma unroll
-      for (int o = 1; o < LPR; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
-      if (r >= nvalid) sc = -INFINITY;
-      const float mnew = fmaxf(m[k], warp_max(sc));
-      const float alpha = exp2f(m[k] - mnew);
-      const float pr = (r < nvalid) ? exp2f(sc - mnew) : 0.f;
-      l[k] = l[k] * alpha + (sub == 0 ? pr : 0.f);
-      m[k] = mnew;
-      const float2 a2 = make_float2(alpha, alpha);
+        for (int o = 1; o < LPR; o <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+        sc = rv ? sc * p.scale_log2 : -INFINITY;
+        const float mnew = fmaxf(m[k], warp_max(sc));
+        const float alpha = ex2_approx(m[k] - mnew);
+        const float pr = rv ? ex2_approx(sc - mnew) : 0.f;
+        l[k] = l[k] * alpha + (sub == 0 ? pr : 0.f);
+        m[k] = mnew;
+        const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
-      for (int i = 0; i < VE / 2; ++i) acc[k][i] = __fmul2_rn(acc[k][i], a2);
+        for (int i = 0; i < VE / 2; ++i) acc[k][i] = __fmul2_rn(acc[k][i], a2);
 #pragma unroll
-      for (int ps = 0; ps < PVP; ++ps) {
-        const int rr = ps * RG + rg;
-        const float prr = __shfl_sync(0xffffffffu, pr, (rr < BS ? rr : 0) * LPR);
-        if (rr < nvalid) {
-          float2 vv[VE / 2];
-          load_f2<T, VE>(Vh + (size_t)rr * HD + cidx * VE, vv);
-          const float2 p2 = make_float2(prr, prr);
+        for (int ps = 0; ps < PVP; ++ps) {
+          const int rr = ps * RG + rg;
+          const float prr = __shfl_sync(0xffffffffu, pr, (rr < BS ? rr : 0) * LPR);
+          if ((FULL && rr < BS) || rr < nvalid) {
+            float2 vv[VE / 2];
+            load_f2<T, VE>(Vh + (size_t)rr * HD + cidx * VE, vv);
+            const float2 p2 = make_float2(prr, prr);
 #pragma unroll
-          for (int i = 0; i < VE / 2; ++i) acc[k][i] = __ffma2_rn(p2, vv[i], acc[k][i]);
+            for (int i = 0; i < VE / 2; ++i) acc[k][i] = __ffma2_rn(p2, vv[i], acc[k][i]);
+          }
         }
       }
-    }
+    };
+    if (nvalid == BS)
+      head_block(std::true_type{});
+    else
+      head_block(std::false_type{});
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     if (++s == S) {

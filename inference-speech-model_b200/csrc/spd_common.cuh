@@ -177,6 +177,14 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// 2^x by the hardware approximation (ex2.approx.ftz: results below 2^-126 are 0, which for
+// softmax weights relative to the running maximum is exact enough); 2^-inf = 0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ---------------------------------------------------------------- warp reductions
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
