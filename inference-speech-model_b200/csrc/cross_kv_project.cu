@@ -10,14 +10,16 @@
 // is computed, with the epilogue writing C straight into the graph-slot layout
 // [S][L][2][H][T_out][D] (no transpose copies).
 //
-// sm_100a design: one 128x256 output tile per CTA (4 warps).  Warp 0 lane 0 issues
-// 2-D TMA loads (128-byte swizzle, no multicast) of the A and W tiles for each 64-wide
-// K slice into a 4-stage shared-memory ring (full/empty mbarriers); warp 1 lane 0
-// issues tcgen05.mma (kind::f16, M=128, N=256, K=16, fp32 accumulator in 256 TMEM
-// columns) and frees each stage with tcgen05.commit; after the last K slice a commit
-// signals the epilogue, where each of the 128 threads owns one accumulator row (TMEM
-// lane), reads it with tcgen05.ld, adds the bias in fp32, rounds and stores 16-byte
-// runs of one head's row.  All waits are bounded (SPD_DEVERR_TIMEOUT on expiry).
+// sm_100a design: a persistent grid (one CTA per SM) walks the 128x256 output tiles.
+// Warp 0 lane 0 issues 2-D TMA loads (128-byte swizzle, no multicast) of the A and W
+// tiles for each 64-wide K slice into a 4-stage shared-memory ring (full/empty
+// mbarriers); warp 1 lane 0 issues tcgen05.mma (kind::f16, M=128, N=256, K=16) into one
+// of two 256-column fp32 TMEM accumulators, frees each stage with tcgen05.commit and
+// signals a finished tile with a commit on that accumulator's barrier; warps 2..5 are
+// the epilogue, one accumulator row (TMEM lane) per thread: tcgen05.ld, the bias in
+// fp32, rounding, and 16-byte stores of one head's row into the slot layout, after which
+// the accumulator is handed back.  So tile i's epilogue overlaps tile i+1's MMAs.  All
+// waits are bounded (SPD_DEVERR_TIMEOUT on expiry).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -115,8 +117,17 @@ __host__ __device__ constexpr uint32_t instr_desc(bool bf16) {
          ((uint32_t)(BM >> 4) << 24);
 }
 
+// Persistent, warp-specialised: CTA c computes tiles c, c + G, c + 2G, ... (G CTAs).
+//   warp 0        TMA producer: A and W K-slices into the STAGES-deep shared ring
+//   warp 1        MMA issuer: each tile into one of two TMEM accumulators (2 x 256 columns)
+//   warps 2..5    epilogue: TMEM -> registers -> bias -> slot layout; warp w reads TMEM
+//                 lanes 32*(w%4).., so the four warps cover the 128 accumulator rows
+// The epilogue of tile i runs while the MMAs of tile i+1 fill the other accumulator.
+constexpr int kProjThreads = 192;
+constexpr int kAccBufs = 2;
+
 template <typename T>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kProjThreads, 1)
     cross_kv_project_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                             const Params p) {
   extern __shared__ unsigned char smem_raw[];
@@ -126,21 +137,26 @@ __global__ void __launch_bounds__(128, 1)
   unsigned char* b_tiles = smem + STAGES * A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(b_tiles + STAGES * B_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_full = empty + STAGES;     // [kAccBufs]: MMAs of a tile done
+  uint64_t* acc_empty = acc_full + kAccBufs;  // [kAccBufs]: epilogue has read the accumulator
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + kAccBufs);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
   const int nk = p.K / BK;
+  const int tiles_n = (p.N + BN - 1) / BN, tiles_m = (p.M + BM - 1) / BM;
+  const int n_tiles = tiles_n * tiles_m;
   constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
 
-  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  if (warp == 1) tmem_alloc(tmem_slot, kAccBufs * TMEM_COLS);
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int b = 0; b < kAccBufs; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
     fence_barrier_init();
   }
   tc_fence_before();
@@ -148,73 +164,109 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ---- TMA producer ------------------------------------------------------------
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % STAGES;
-      if (kb >= STAGES && !mbar_wait_bounded(&empty[s], ((kb / STAGES) & 1) ^ 1, p.err)) break;
-      mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
-      tma_load_2d(a_tiles + s * A_BYTES, &tm_a, kb * BK, m0, &full[s]);
-      tma_load_2d(b_tiles + s * B_BYTES, &tm_b, kb * BK, n0, &full[s]);
+  if (warp == 0) {
+    // ---- TMA producer --------------------------------------------------------------
+    if (lane == 0) {
+      long long it = 0;  // K-slices issued, over all tiles
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+        const int n0 = (tile % tiles_n) * BN, m0 = (tile / tiles_n) * BM;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = (int)(it % STAGES);
+          if (it >= STAGES && !mbar_wait_bounded(&empty[s], (uint32_t)(((it / STAGES) & 1) ^ 1), p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+          tma_load_2d(a_tiles + s * A_BYTES, &tm_a, kb * BK, m0, &full[s]);
+          tma_load_2d(b_tiles + s * B_BYTES, &tm_b, kb * BK, n0, &full[s]);
+        }
+      }
+      if (!ok)  // let the copies in flight land before the CTA can exit
+        for (long long k = it - 1; k >= 0 && k >= it - STAGES; --k)
+          (void)mbar_wait_bounded(&full[k % STAGES], (uint32_t)((k / STAGES) & 1), nullptr);
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {
     // ---- MMA issuer ----------------------------------------------------------------
-    constexpr uint32_t idesc = instr_desc(kBf16);
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % STAGES;
-      if (!mbar_wait_bounded(&full[s], (kb / STAGES) & 1, p.err)) break;
-      tc_fence_after();
-      const uint64_t da = smem_desc_sw128(a_tiles + s * A_BYTES);
-      const uint64_t db = smem_desc_sw128(b_tiles + s * B_BYTES);
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(kBf16);
+      long long it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local % kAccBufs;
+        const int use = local / kAccBufs;
+        if (use > 0 && !mbar_wait_bounded(&acc_empty[buf], (uint32_t)((use - 1) & 1), p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(buf * TMEM_COLS);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = (int)(it % STAGES);
+          if (!mbar_wait_bounded(&full[s], (uint32_t)((it / STAGES) & 1), p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_sw128(a_tiles + s * A_BYTES);
+          const uint64_t db = smem_desc_sw128(b_tiles + s * B_BYTES);
 #pragma unroll
-      for (int k = 0; k < BK / 16; ++k) {
-        // each K=16 step advances 32 bytes inside the 128-byte swizzle row
-        umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          for (int k = 0; k < BK / 16; ++k) {
+            // each K=16 step advances 32 bytes inside the 128-byte swizzle row
+            umma_f16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[buf]);
       }
-      umma_commit(&empty[s]);
     }
-    umma_commit(acc_full);
-  }
-  __syncwarp();
-
-  // ---- epilogue: thread = accumulator row (TMEM lane 32*warp + lane) --------------------
-  const bool ready = mbar_wait_bounded(acc_full, 0, p.err);
-  __syncwarp();
-  tc_fence_after();
-  const int m = m0 + warp * 32 + lane;
-  const bool row_ok = ready && m < p.M;
-  const int b = row_ok ? m / p.T : 0;
-  const int t = row_ok ? m % p.T : 0;
-  const long long slot = row_ok ? (p.slot_ids ? p.slot_ids[b] : b) : 0;
-  T* out = reinterpret_cast<T*>(p.out) + slot * p.out_slot_stride + (long long)t * p.D;
-  const T* bias = reinterpret_cast<const T*>(p.bias);
-  const int HD = p.H * p.D;
-  const long long plane = (long long)p.T_out * p.D;  // one (layer, k|v, head) plane
+  } else {
+    // ---- epilogue: thread = accumulator row (TMEM lane 32*(warp%4) + lane) ---------------
+    const int q = warp & 3;
+    const T* bias = reinterpret_cast<const T*>(p.bias);
+    const int HD = p.H * p.D;
+    const long long plane = (long long)p.T_out * p.D;  // one (layer, k|v, head) plane
+    int local = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
+      const int buf = local % kAccBufs;
+      const int n0 = (tile % tiles_n) * BN, m0 = (tile / tiles_n) * BM;
+      const bool ready = mbar_wait_bounded(&acc_full[buf], (uint32_t)((local / kAccBufs) & 1), p.err);
+      if (!__all_sync(0xffffffffu, ready)) break;
+      tc_fence_after();
+      const int m = m0 + q * 32 + lane;
+      const bool row_ok = m < p.M;
+      const int b = row_ok ? m / p.T : 0;
+      const int t = row_ok ? m % p.T : 0;
+      const long long slot = row_ok ? (p.slot_ids ? p.slot_ids[b] : b) : 0;
+      T* out = reinterpret_cast<T*>(p.out) + slot * p.out_slot_stride + (long long)t * p.D;
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 16) {
-    float v[16];
-    tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);  // all lanes, aligned
-    if (!row_ok) continue;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TMEM_COLS + c0), v);  // all lanes
+        if (!row_ok) continue;
 #pragma unroll
-    for (int g = 0; g < 16; g += 8) {
-      const int n = n0 + c0 + g;
-      if (n >= p.N) break;
-      const int lkv = n / HD, rem = n % HD;
-      const int h = rem / p.D, d = rem % p.D;
-      alignas(16) T o[8];
+        for (int g = 0; g < 16; g += 8) {
+          const int n = n0 + c0 + g;
+          if (n >= p.N) break;
+          const int lkv = n / HD, rem = n % HD;
+          const int h = rem / p.D, d = rem % p.D;
+          alignas(16) T o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float x = v[g + i];
-        if (bias) x += Elem<T>::to_f(bias[n + i]);
-        o[i] = Elem<T>::from_f(x);
+          for (int i = 0; i < 8; ++i) {
+            float x = v[g + i];
+            if (bias) x += Elem<T>::to_f(bias[n + i]);
+            o[i] = Elem<T>::from_f(x);
+          }
+          *reinterpret_cast<uint4*>(out + ((long long)lkv * p.H + h) * plane + d) = *reinterpret_cast<uint4*>(o);
+        }
       }
-      *reinterpret_cast<uint4*>(out + ((long long)lkv * p.H + h) * plane + d) = *reinterpret_cast<uint4*>(o);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+  if (warp == 1) tmem_dealloc(tmem, kAccBufs * TMEM_COLS);
 }
 
 // ---- host side ------------------------------------------------------------------------
@@ -249,8 +301,8 @@ bool make_map(CUtensorMap* map, const void* base, int inner, int rows, int box_r
 int cross_kv_project_launch(const void* enc_out, const void* w_kv, const void* b_kv, void* out,
                             const int32_t* slot_ids, int B, int T, int d_model, int L, int H, int D, int T_out,
                             int64_t out_slot_stride, int dtype, int* err, int sms, cudaStream_t st) {
-  (void)sms;
   using namespace proj;
+  if (sms < 1) sms = 1;
   const bool bf16 = dtype == SPD_BF16;
   const long long M = (long long)B * T, N = (long long)L * 2 * H * D;
   if (M > (1ll << 31) - 1 || N > (1ll << 31) - 1 || (N % 8)) return SPD_ERR_UNSUPPORTED;
@@ -261,17 +313,18 @@ int cross_kv_project_launch(const void* enc_out, const void* w_kv, const void* b
   p.bias = b_kv; p.out = out; p.slot_ids = slot_ids;
   p.M = (int)M; p.N = (int)N; p.K = d_model; p.T = T; p.H = H; p.D = D; p.T_out = T_out;
   p.out_slot_stride = out_slot_stride; p.err = err;
-  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
+  const long long tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM);
+  dim3 grid((unsigned)(tiles < sms ? tiles : sms));  // persistent: at most one CTA per SM
   if (bf16) {
     auto k = cross_kv_project_kernel<__nv_bfloat16>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess)
       return SPD_ERR_CUDA;
-    k<<<grid, 128, SMEM_BYTES, st>>>(ta, tb, p);
+    k<<<grid, kProjThreads, SMEM_BYTES, st>>>(ta, tb, p);
   } else {
     auto k = cross_kv_project_kernel<__half>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess)
       return SPD_ERR_CUDA;
-    k<<<grid, 128, SMEM_BYTES, st>>>(ta, tb, p);
+    k<<<grid, kProjThreads, SMEM_BYTES, st>>>(ta, tb, p);
   }
   return cudaPeekAtLastError() == cudaSuccess ? SPD_OK : SPD_ERR_CUDA;
 }

@@ -98,9 +98,6 @@ __device__ __forceinline__ void load_f2(const T* p, float2* out) {
   }
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
 
 template <typename T, int D, int BS>
 struct PagedGeom {
