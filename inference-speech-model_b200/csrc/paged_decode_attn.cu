@@ -123,9 +123,14 @@ struct StageMeta {
   int flags;  // kFirst | kLast
 };
 constexpr int kFirst = 1, kLast = 2;
+constexpr int kPairThreads = 416;  // two-CTA form: up to 12 compute warps + the producer
+constexpr int kPairMinSeqs = 128;  // batches at least this large use the two-CTA form
 
-template <typename T, int D, int BS, int HPW>
-__global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParams p) {
+// PAIR: the two-CTAs-per-SM form (at most 12 compute warps, registers capped for two
+// resident CTAs, compact stages: the append rows are copied into the staged block).
+template <typename T, int D, int BS, int HPW, bool PAIR>
+__global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
+    paged_decode_attn_kernel(const PagedParams p) {
   using Gm = PagedGeom<T, D, BS>;
   constexpr int LPR = Gm::LPR, DPL = Gm::DPL, CH = Gm::CH, NCH = Gm::NCH;
   constexpr int VE = Gm::VE, CPR = Gm::CPR, RG = Gm::RG, PVP = Gm::PVP;
@@ -138,7 +143,8 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   // ---- shared memory: ring | barriers | metadata | lengths | item prefix | table ----
-  const size_t stage_elems = 2 * unit_elems + 3 * (size_t)HD;  // K, V, q, k_new, v_new
+  // K, V, q (and, in the single-CTA form, k_new / v_new rows for the fused append)
+  const size_t stage_elems = 2 * unit_elems + (PAIR ? 1 : 3) * (size_t)HD;
   T* ring = reinterpret_cast<T*>(smem);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + round_up((size_t)S * stage_elems * sizeof(T), 128));
   uint64_t* empty = full + S;
@@ -261,18 +267,37 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
           const bool app = append && (j == nblk - 1);
           meta[s] = StageMeta{b, j, item, (first ? kFirst : 0) | (last ? kLast : 0)};
           const size_t off = (size_t)phys * unit_elems;
-          const uint32_t bytes = (uint32_t)(nvalid * HD * (int)sizeof(T));
           const uint32_t row_bytes = (uint32_t)(HD * (int)sizeof(T));
           T* dst = ring + (size_t)s * stage_elems;
-          mbar_arrive_expect_tx(&full[s], 2 * bytes + (first ? row_bytes : 0u) + (app ? 2 * row_bytes : 0u));
-          bulk_copy_g2s(dst, kpool + off, bytes, &full[s]);
-          bulk_copy_g2s(dst + unit_elems, vpool + off, bytes, &full[s]);
-          if (first) bulk_copy_g2s(dst + 2 * unit_elems, qg + (size_t)b * HD, row_bytes, &full[s]);
-          if (app) {
-            bulk_copy_g2s(dst + 2 * unit_elems + HD, reinterpret_cast<const T*>(p.k_new) + (size_t)b * HD,
-                          row_bytes, &full[s]);
-            bulk_copy_g2s(dst + 2 * unit_elems + 2 * HD, reinterpret_cast<const T*>(p.v_new) + (size_t)b * HD,
-                          row_bytes, &full[s]);
+          if constexpr (PAIR) {
+            // compact stages: the new row (nvalid-1) comes from k_new / v_new straight into
+            // its place, the pool supplies the rows before it
+            const int npool = app ? nvalid - 1 : nvalid;
+            const uint32_t bytes = (uint32_t)npool * row_bytes;
+            mbar_arrive_expect_tx(&full[s], 2 * bytes + (first ? row_bytes : 0u) + (app ? 2 * row_bytes : 0u));
+            if (npool > 0) {
+              bulk_copy_g2s(dst, kpool + off, bytes, &full[s]);
+              bulk_copy_g2s(dst + unit_elems, vpool + off, bytes, &full[s]);
+            }
+            if (first) bulk_copy_g2s(dst + 2 * unit_elems, qg + (size_t)b * HD, row_bytes, &full[s]);
+            if (app) {
+              bulk_copy_g2s(dst + (size_t)(nvalid - 1) * HD, reinterpret_cast<const T*>(p.k_new) + (size_t)b * HD,
+                            row_bytes, &full[s]);
+              bulk_copy_g2s(dst + unit_elems + (size_t)(nvalid - 1) * HD,
+                            reinterpret_cast<const T*>(p.v_new) + (size_t)b * HD, row_bytes, &full[s]);
+            }
+          } else {
+            const uint32_t bytes = (uint32_t)(nvalid * HD * (int)sizeof(T));
+            mbar_arrive_expect_tx(&full[s], 2 * bytes + (first ? row_bytes : 0u) + (app ? 2 * row_bytes : 0u));
+            bulk_copy_g2s(dst, kpool + off, bytes, &full[s]);
+            bulk_copy_g2s(dst + unit_elems, vpool + off, bytes, &full[s]);
+            if (first) bulk_copy_g2s(dst + 2 * unit_elems, qg + (size_t)b * HD, row_bytes, &full[s]);
+            if (app) {
+              bulk_copy_g2s(dst + 2 * unit_elems + HD, reinterpret_cast<const T*>(p.k_new) + (size_t)b * HD,
+                            row_bytes, &full[s]);
+              bulk_copy_g2s(dst + 2 * unit_elems + 2 * HD, reinterpret_cast<const T*>(p.v_new) + (size_t)b * HD,
+                            row_bytes, &full[s]);
+            }
           }
           if (n_issued == 0) SPD_TRACE(2);
           ++n_issued;
@@ -374,15 +399,22 @@ __global__ void __launch_bounds__(544) paged_decode_attn_kernel(const PagedParam
         if (h >= H) break;
         for (int i = lane * VEC; i < D; i += 32 * VEC) {
           const size_t e = row_off + (size_t)h * D + i;
-          const uint4 kv = *reinterpret_cast<const uint4*>(Qs + HD + h * D + i);
-          const uint4 vv = *reinterpret_cast<const uint4*>(Qs + 2 * HD + h * D + i);
-          *reinterpret_cast<uint4*>(Ks + e) = kv;
-          *reinterpret_cast<uint4*>(Vs + e) = vv;
-          *reinterpret_cast<uint4*>(const_cast<T*>(kpool) + (size_t)phys * unit_elems + e) = kv;
-          *reinterpret_cast<uint4*>(const_cast<T*>(vpool) + (size_t)phys * unit_elems + e) = vv;
+          if constexpr (PAIR) {  // the new row arrived in its place in the staged block
+            *reinterpret_cast<uint4*>(const_cast<T*>(kpool) + (size_t)phys * unit_elems + e) =
+                *reinterpret_cast<const uint4*>(Ks + e);
+            *reinterpret_cast<uint4*>(const_cast<T*>(vpool) + (size_t)phys * unit_elems + e) =
+                *reinterpret_cast<const uint4*>(Vs + e);
+          } else {  // fill the new row's place in the staged block, and the pool
+            const uint4 kv = *reinterpret_cast<const uint4*>(Qs + HD + h * D + i);
+            const uint4 vv = *reinterpret_cast<const uint4*>(Qs + 2 * HD + h * D + i);
+            *reinterpret_cast<uint4*>(Ks + e) = kv;
+            *reinterpret_cast<uint4*>(Vs + e) = vv;
+            *reinterpret_cast<uint4*>(const_cast<T*>(kpool) + (size_t)phys * unit_elems + e) = kv;
+            *reinterpret_cast<uint4*>(const_cast<T*>(vpool) + (size_t)phys * unit_elems + e) = vv;
+          }
         }
       }
-      fence_proxy_async_smem();  // generic writes before the next bulk copy into this stage
+      if constexpr (!PAIR) fence_proxy_async_smem();  // generic writes before the next bulk copy into this stage
       __syncwarp();
     }
 
@@ -589,12 +621,13 @@ static int launch_merge(const PagedParams& p, cudaStream_t stream) {
   return cudaLaunchKernelEx(&cfg, paged_merge_kernel<T, D, BS>, p) == cudaSuccess ? SPD_OK : SPD_ERR_CUDA;
 }
 
-template <typename T, int D, int BS, int HPW>
+template <typename T, int D, int BS, int HPW, bool PAIR>
 static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t stream) {
   PagedParams p = base;
   const int nw = (p.H + HPW - 1) / HPW;
   const int threads = (nw + 1) * 32;  // compute warps + producer warp
-  const size_t stage_bytes = ((size_t)2 * BS + 3) * p.H * D * sizeof(T);
+  if (PAIR && threads > kPairThreads) return SPD_ERR_UNSUPPORTED;
+  const size_t stage_bytes = ((size_t)2 * BS + (PAIR ? 1 : 3)) * p.H * D * sizeof(T);
   const size_t tab_bytes = (size_t)p.B * p.max_blocks * 4;
   p.table_in_smem = (tab_bytes <= kTableSmemMax && tab_bytes % 16 == 0 &&
                      (reinterpret_cast<uintptr_t>(p.block_tables) & 15) == 0)
@@ -604,21 +637,23 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
                        (p.table_in_smem ? tab_bytes : 0) + 256;
   // Ring depth: up to ~216 KB per CTA (one CTA per SM at the Whisper shapes; the
   // producer warp keeps every stage in flight), at least two stages.
-  int S = (int)((216 * 1024 > fixed ? 216 * 1024 - fixed : 0) / stage_bytes);
+  const size_t budget = (PAIR ? 112 : 216) * 1024;
+  int S = (int)((budget > fixed ? budget - fixed : 0) / stage_bytes);
   if (S < 2 && 2 * stage_bytes + fixed <= 227 * 1024) S = 2;
   S = S < 1 ? 1 : (S > 8 ? 8 : S);
   p.stages = S;
   const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * ((size_t)S * 2 + 2) + 16 * (size_t)S + 16 +
                       4 * ((((size_t)p.B + 3) & ~(size_t)3) + (((size_t)p.B + 4) & ~(size_t)3)) +
                       (p.table_in_smem ? tab_bytes : 0);
-  if (smem > 227 * 1024) return SPD_ERR_UNSUPPORTED;
-  auto kfn = paged_decode_attn_kernel<T, D, BS, HPW>;
+  if (smem > (PAIR ? 113 : 227) * 1024) return SPD_ERR_UNSUPPORTED;
+  auto kfn = paged_decode_attn_kernel<T, D, BS, HPW, PAIR>;
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return SPD_ERR_CUDA;
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kfn, threads, smem) != cudaSuccess || occ < 1)
     return SPD_ERR_CUDA;
+  if (PAIR && occ < 2) return SPD_ERR_UNSUPPORTED;
   if (occ > kMaxCtasPerSm) occ = kMaxCtasPerSm;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(device_sms * occ));
@@ -634,16 +669,26 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
   return launch_merge<T, D, BS>(p, stream);
 }
 
+template <typename T, int D, int BS>
+static int launch_paged_bs(const PagedParams& p, int sms, cudaStream_t st) {
+  if (p.H > 16) return launch_paged<T, D, BS, 2, false>(p, sms, st);
+  // Large batches: two CTAs per SM (twice the compute warps to hide the per-block
+  // latency, more bytes in flight).  Small ones keep one CTA per SM: with fewer items per
+  // CTA the per-CTA set-up costs more than the extra warps save.
+  if (p.B >= kPairMinSeqs) {
+    const int rc = launch_paged<T, D, BS, 1, true>(p, sms, st);
+    if (rc != SPD_ERR_UNSUPPORTED) return rc;
+  }
+  return launch_paged<T, D, BS, 1, false>(p, sms, st);
+}
+
 template <typename T, int D>
 static int dispatch_bs(const PagedParams& p, int bs, int sms, cudaStream_t st) {
-  const bool two = p.H > 16;
   switch (bs) {
-    case 8: return two ? launch_paged<T, D, 8, 2>(p, sms, st) : launch_paged<T, D, 8, 1>(p, sms, st);
-    case 16: return two ? launch_paged<T, D, 16, 2>(p, sms, st) : launch_paged<T, D, 16, 1>(p, sms, st);
+    case 8: return launch_paged_bs<T, D, 8>(p, sms, st);
+    case 16: return launch_paged_bs<T, D, 16>(p, sms, st);
     case 32:
-      if constexpr (D <= 64) {
-        return two ? launch_paged<T, D, 32, 2>(p, sms, st) : launch_paged<T, D, 32, 1>(p, sms, st);
-      }
+      if constexpr (D <= 64) return launch_paged_bs<T, D, 32>(p, sms, st);
       return SPD_ERR_UNSUPPORTED;
     default: return SPD_ERR_UNSUPPORTED;
   }

@@ -136,12 +136,13 @@ def test_paged_attention_config2_full_size():
     assert _err(out, ref) <= ATOL_16
 
 
-@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_fused_append_writes_row_and_attends_to_it(dtype):
+@pytest.mark.parametrize("dtype,B", [(torch.float16, 5), (torch.bfloat16, 5), (torch.float16, 160)])
+def test_fused_append_writes_row_and_attends_to_it(dtype, B):
+    """B=160 runs the two-CTAs-per-SM form, whose stages take the new row by copy."""
     rng = np.random.default_rng(11)
-    B, H, D, bs = 5, 12, 64, 16
-    ctx = np.array([1, 16, 17, 100, 33], np.int32)
-    nb = 64
+    H, D, bs = 12, 64, 16
+    ctx = np.array([1, 16, 17, 100, 33], np.int32) if B == 5 else rng.integers(1, 300, B).astype(np.int32)
+    nb = int(sum(-(-int(c) // bs) for c in ctx)) + 8
     tq, tk, tv, tt, tc, q, kp, vp, tables = _random_paged(rng, B, H, D, bs, nb, ctx, dtype)
     k_new = (torch.randn(B, H, D) * 0.5).to(dtype).to(DEV)
     v_new = (torch.randn(B, H, D) * 0.5).to(dtype).to(DEV)
