@@ -33,6 +33,38 @@ from . import ops
 os.environ.setdefault("USE_TF", "0")
 
 
+def _fused_qkv(model: nn.Module, projs, q_scale: float = 1.0):
+    """Per layer, the q / k / v projection weights stacked for one batched GEMM:
+    (W [3, d_in, H*D] with W[i] = weight_i^T, bias [3, 1, H*D] (zeros where a projection
+    has none)); the q rows are multiplied by ``q_scale``.  Built on first use and rebuilt
+    when a weight has been replaced or modified in place."""
+    key = tuple((p.weight.data_ptr(), p.weight._version) for trio in projs for p in trio) + (q_scale,)
+    cache = model.__dict__.get("_qkv_cache")
+    if cache is not None and cache[0] == key:
+        return cache[1]
+    out = []
+    with torch.no_grad():
+        for qp, kp, vp in projs:
+            w = torch.stack([qp.weight * q_scale, kp.weight, vp.weight]).transpose(1, 2).contiguous()
+            bs = [qp.bias * q_scale if qp.bias is not None else None, kp.bias, vp.bias]
+            bias = torch.stack([b if b is not None else torch.zeros_like(qp.weight[:, 0]) for b in bs]).unsqueeze(1)
+            out.append((w, bias))
+    model.__dict__["_qkv_cache"] = (key, out)
+    return out
+
+
+def _scaled_linears(model: nn.Module, linears, scale: float):
+    """(weight * scale, bias * scale) per Linear, cached like ``_fused_qkv``."""
+    key = tuple((p.weight.data_ptr(), p.weight._version) for p in linears) + (scale,)
+    cache = model.__dict__.get("_scaled_cache")
+    if cache is not None and cache[0] == key:
+        return cache[1]
+    with torch.no_grad():
+        out = [(p.weight * scale, p.bias * scale if p.bias is not None else None) for p in linears]
+    model.__dict__["_scaled_cache"] = (key, out)
+    return out
+
+
 class _LayerKV:
     """Keys/values of one decoder layer ([B, H, T, D]), named like a DynamicCache layer."""
 
@@ -208,11 +240,12 @@ class WhisperClassSpeechEncoderDecoderModel(nn.Module):
         x = self.decoder_embed(st.token_ids[:n]).to(self.dtype)  # [n, d]
         H, D = self.num_heads, self.head_dim
         scale = 1.0 / math.sqrt(D)
+        fused = _fused_qkv(self, [(lay.self_attn_q, lay.self_attn_k, lay.self_attn_v) for lay in self.decoder_layers])
         for l, layer in enumerate(self.decoder_layers):
             h = layer.norm1(x)
-            q = layer.self_attn_q(h).view(n, H, D)
-            k = layer.self_attn_k(h).view(n, H, D)
-            v = layer.self_attn_v(h).view(n, H, D)
+            w, _ = fused[l]
+            qkv = torch.bmm(h.unsqueeze(0).expand(3, n, h.shape[-1]), w)  # [3, n, H*D]: q, k, v
+            q, k, v = qkv[0].view(n, H, D), qkv[1].view(n, H, D), qkv[2].view(n, H, D)
             a = ops.paged_decode_attention(q, st.key_pool[l], st.value_pool[l], st.block_tables[:n], st.ctx_lens[:n],
                                            scale=scale, k_new=k, v_new=v, workspace=st.paged_ws[n])
             x = x + layer.self_attn_out(a.view(n, -1))
@@ -415,17 +448,29 @@ class PretrainedWhisperModel(nn.Module):
         H, D = self.num_heads, self.head_dim
         pos = (st.ctx_lens[:n] - 1).clamp_(min=0).long()
         x = dec.embed_tokens(st.token_ids[:n]) * dec.embed_scale + dec.embed_positions.weight[pos]
+        # q, k and v of a layer as one batched GEMM; WhisperAttention's query scaling is
+        # folded into the q weights when it is a power of two (exact), else applied after
+        fold = math.log2(dec.layers[0].self_attn.scaling).is_integer()
+        fused = _fused_qkv(self, [(lay.self_attn.q_proj, lay.self_attn.k_proj, lay.self_attn.v_proj)
+                                  for lay in dec.layers], q_scale=dec.layers[0].self_attn.scaling if fold else 1.0)
+        cross_q = _scaled_linears(self, [lay.encoder_attn.q_proj for lay in dec.layers],
+                                  dec.layers[0].encoder_attn.scaling) if fold else None
         for l, layer in enumerate(dec.layers):
             sa = layer.self_attn
             h = layer.self_attn_layer_norm(x)
-            q = (sa.q_proj(h) * sa.scaling).view(n, H, D)
-            k = sa.k_proj(h).view(n, H, D)
-            v = sa.v_proj(h).view(n, H, D)
+            w, bias = fused[l]
+            qkv = torch.baddbmm(bias, h.unsqueeze(0).expand(3, n, h.shape[-1]), w)  # [3, n, H*D]
+            q = qkv[0] if fold else qkv[0] * sa.scaling
+            q, k, v = q.view(n, H, D), qkv[1].view(n, H, D), qkv[2].view(n, H, D)
             a = ops.paged_decode_attention(q, st.key_pool[l], st.value_pool[l], st.block_tables[:n], st.ctx_lens[:n],
                                            scale=1.0, k_new=k, v_new=v, workspace=st.paged_ws[n])
             x = x + sa.out_proj(a.view(n, -1))
             ea = layer.encoder_attn
-            cq = (ea.q_proj(layer.encoder_attn_layer_norm(x)) * ea.scaling).view(n, H, D)
+            if fold:
+                wq, bq = cross_q[l]
+                cq = F.linear(layer.encoder_attn_layer_norm(x), wq, bq).view(n, H, D)
+            else:
+                cq = (ea.q_proj(layer.encoder_attn_layer_norm(x)) * ea.scaling).view(n, H, D)
             c = ops.cross_attention(cq, st.cross_kv[:n, l, 0], st.cross_kv[:n, l, 1], st.cross_lens[:n], scale=1.0,
                                     workspace=st.cross_ws[n])
             x = x + ea.out_proj(c.view(n, -1))
