@@ -33,6 +33,9 @@
  *                          (pool[table].view(-1,H,D)[:T].permute(1,0,2), zero padded)
  *   spd_cross_kv_project   speech_serving/models.py:554-561 (per-decoder-layer
  *                          encoder_attn.k_proj / v_proj over the encoder output)
+ *   spd_add_layernorm      the residual add and the LayerNorm after it in every decoder
+ *                          layer, speech_serving/models.py:163-207 (x = residual + ...;
+ *                          norm2 / norm3), and transformers' WhisperDecoderLayer
  */
 #ifndef SPD_B200_H
 #define SPD_B200_H
@@ -153,6 +156,15 @@ int spd_cross_kv_project(const void* enc_out, const void* w_kv, const void* b_kv
                          const int32_t* slot_ids, int B, int T, int d_model, int L, int H,
                          int D, int T_out, int64_t out_slot_stride, int dtype,
                          int32_t* error_word, void* stream);
+
+/* Residual add fused with the LayerNorm that follows it (decoder-layer glue around the
+ * kernels above), one warp per row of `cols` elements (cols * element size a multiple
+ * of 16 bytes, cols <= 2048):
+ *   x_out[r] = round(x[r] + delta[r])                          (delta NULL: x_out unused)
+ *   y[r]     = round((x_out[r] - mean) / sqrt(var + eps) * gamma + beta)
+ * mean and var (biased) in fp32 over the rounded x_out; x_out may alias x. */
+int spd_add_layernorm(const void* x, const void* delta, const void* gamma, const void* beta,
+                      void* x_out, void* y, int rows, int cols, float eps, int dtype, void* stream);
 
 /* Allocation-free variant of spd_paged_decode_attn, for callers that cannot allocate
  * GPU memory or own a workspace: code running where cudaMalloc is unavailable or

@@ -16,6 +16,7 @@ int paged_decode_attn_launch(const PagedParams& p, int dtype, int D, int bs, int
 int cross_attn_launch(const CrossParams& p, int dtype, int D, int sms, cudaStream_t st);
 int kv_append_launch(const AppendParams& p, int sms, cudaStream_t st);
 int block_gather_launch(const GatherParams& p, int sms, cudaStream_t st);
+int add_layernorm_launch(const AddLnParams& p, int dtype, cudaStream_t st);
 int cross_kv_project_launch(const void* enc_out, const void* w_kv, const void* b_kv, void* out,
                             const int32_t* slot_ids, int B, int T, int d_model, int L, int H, int D,
                             int T_out, int64_t out_slot_stride, int dtype, int* err, int sms, cudaStream_t st);
@@ -248,6 +249,24 @@ int spd_block_gather(const void* pool, const int32_t* block_tables, const int32_
   p.out_batch_stride = out_batch_stride * eb; p.err = error_word;
   const int rc = spd::block_gather_launch(p, sms, static_cast<cudaStream_t>(stream));
   if (rc != SPD_OK) return fail(rc, "spd_block_gather: launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return ok();
+}
+
+int spd_add_layernorm(const void* x, const void* delta, const void* gamma, const void* beta, void* x_out, void* y,
+                      int rows, int cols, float eps, int dtype, void* stream) {
+  const int eb = elem_bytes(dtype);
+  if (!eb) return fail(SPD_ERR_UNSUPPORTED, "spd_add_layernorm: dtype %d not supported", dtype);
+  if (!x || !gamma || !beta || !y || (delta && !x_out)) return fail(SPD_ERR_INVALID_ARG, "spd_add_layernorm: null pointer");
+  if (rows < 0 || cols <= 0) return fail(SPD_ERR_INVALID_ARG, "spd_add_layernorm: bad sizes");
+  if ((cols * eb) % 16 || !aligned16(x) || !aligned16(gamma) || !aligned16(beta) || !aligned16(y) ||
+      (delta && (!aligned16(delta) || !aligned16(x_out))))
+    return fail(SPD_ERR_INVALID_ARG, "spd_add_layernorm: rows and pointers must be 16-byte aligned");
+  if (cols > 2048) return fail(SPD_ERR_UNSUPPORTED, "spd_add_layernorm: rows of at most 2048 elements");
+  if (rows == 0) return ok();
+  spd::AddLnParams p{x, delta, gamma, beta, x_out, y, rows, cols, eps};
+  const int rc = spd::add_layernorm_launch(p, dtype, static_cast<cudaStream_t>(stream));
+  if (rc == SPD_ERR_UNSUPPORTED) return fail(rc, "spd_add_layernorm: row length not supported");
+  if (rc != SPD_OK) return fail(rc, "spd_add_layernorm: launch failed: %s", cudaGetErrorString(cudaGetLastError()));
   return ok();
 }
 

@@ -52,6 +52,17 @@ struct AppendParams {
   int* err;
 };
 
+struct AddLnParams {  // residual add + LayerNorm (decoder_layer_ops.cu)
+  const void* x;
+  const void* delta;  // or null: y = LayerNorm(x), x_out not written
+  const void* gamma;
+  const void* beta;
+  void* x_out;
+  void* y;
+  int rows, cols;
+  float eps;
+};
+
 struct GatherParams {
   const unsigned char* pool;
   const int* block_tables;

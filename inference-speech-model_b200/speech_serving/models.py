@@ -65,6 +65,24 @@ def _scaled_linears(model: nn.Module, linears, scale: float):
     return out
 
 
+def _padded_head(model: nn.Module, linear: nn.Linear, multiple: int = 64) -> torch.Tensor:
+    """The output projection's weight with its rows (the vocabulary) padded with zeros to a
+    multiple of ``multiple``, so the per-step head GEMM gets an aligned output row; the
+    caller drops the padded columns.  Cached like ``_fused_qkv``."""
+    w = linear.weight
+    key = (w.data_ptr(), w._version, multiple)
+    cache = model.__dict__.get("_head_cache")
+    if cache is not None and cache[0] == key:
+        return cache[1]
+    v = w.shape[0]
+    vp = (v + multiple - 1) // multiple * multiple
+    with torch.no_grad():
+        wp = torch.zeros((vp, w.shape[1]), dtype=w.dtype, device=w.device)
+        wp[:v].copy_(w)
+    model.__dict__["_head_cache"] = (key, wp)
+    return wp
+
+
 class _LayerKV:
     """Keys/values of one decoder layer ([B, H, T, D]), named like a DynamicCache layer."""
 
@@ -241,20 +259,23 @@ class WhisperClassSpeechEncoderDecoderModel(nn.Module):
         H, D = self.num_heads, self.head_dim
         scale = 1.0 / math.sqrt(D)
         fused = _fused_qkv(self, [(lay.self_attn_q, lay.self_attn_k, lay.self_attn_v) for lay in self.decoder_layers])
-        for l, layer in enumerate(self.decoder_layers):
-            h = layer.norm1(x)
+        layers = self.decoder_layers
+        # each residual add runs fused with the LayerNorm after it (x is updated in place)
+        x, h = ops.add_layernorm(x, None, layers[0].norm1)
+        for l, layer in enumerate(layers):
             w, _ = fused[l]
             qkv = torch.bmm(h.unsqueeze(0).expand(3, n, h.shape[-1]), w)  # [3, n, H*D]: q, k, v
             q, k, v = qkv[0].view(n, H, D), qkv[1].view(n, H, D), qkv[2].view(n, H, D)
             a = ops.paged_decode_attention(q, st.key_pool[l], st.value_pool[l], st.block_tables[:n], st.ctx_lens[:n],
                                            scale=scale, k_new=k, v_new=v, workspace=st.paged_ws[n])
-            x = x + layer.self_attn_out(a.view(n, -1))
-            cq = layer.cross_attn_q(layer.norm2(x)).view(n, H, D)
+            x, h = ops.add_layernorm(x, layer.self_attn_out(a.view(n, -1)), layer.norm2)
+            cq = layer.cross_attn_q(h).view(n, H, D)
             c = ops.cross_attention(cq, st.cross_kv[:n, l, 0], st.cross_kv[:n, l, 1], st.cross_lens[:n], scale=scale,
                                     workspace=st.cross_ws[n])
-            x = x + layer.cross_attn_out(c.view(n, -1))
-            x = x + layer.mlp(layer.norm3(x))
-        logits = self.lm_head(self.decoder_norm(x))
+            x, h = ops.add_layernorm(x, layer.cross_attn_out(c.view(n, -1)), layer.norm3)
+            nxt = layers[l + 1].norm1 if l + 1 < len(layers) else self.decoder_norm
+            x, h = ops.add_layernorm(x, layer.mlp(h), nxt)
+        logits = F.linear(h, _padded_head(self, self.lm_head))[:, : self.vocab_size]
         return torch.argmax(logits, dim=-1)
 
 
@@ -455,28 +476,30 @@ class PretrainedWhisperModel(nn.Module):
                                   for lay in dec.layers], q_scale=dec.layers[0].self_attn.scaling if fold else 1.0)
         cross_q = _scaled_linears(self, [lay.encoder_attn.q_proj for lay in dec.layers],
                                   dec.layers[0].encoder_attn.scaling) if fold else None
-        for l, layer in enumerate(dec.layers):
+        layers = dec.layers
+        # each residual add runs fused with the LayerNorm after it (x is updated in place)
+        x, h = ops.add_layernorm(x.contiguous(), None, layers[0].self_attn_layer_norm)
+        for l, layer in enumerate(layers):
             sa = layer.self_attn
-            h = layer.self_attn_layer_norm(x)
             w, bias = fused[l]
             qkv = torch.baddbmm(bias, h.unsqueeze(0).expand(3, n, h.shape[-1]), w)  # [3, n, H*D]
             q = qkv[0] if fold else qkv[0] * sa.scaling
             q, k, v = q.view(n, H, D), qkv[1].view(n, H, D), qkv[2].view(n, H, D)
             a = ops.paged_decode_attention(q, st.key_pool[l], st.value_pool[l], st.block_tables[:n], st.ctx_lens[:n],
                                            scale=1.0, k_new=k, v_new=v, workspace=st.paged_ws[n])
-            x = x + sa.out_proj(a.view(n, -1))
+            x, h = ops.add_layernorm(x, sa.out_proj(a.view(n, -1)), layer.encoder_attn_layer_norm)
             ea = layer.encoder_attn
             if fold:
                 wq, bq = cross_q[l]
-                cq = F.linear(layer.encoder_attn_layer_norm(x), wq, bq).view(n, H, D)
+                cq = F.linear(h, wq, bq).view(n, H, D)
             else:
-                cq = (ea.q_proj(layer.encoder_attn_layer_norm(x)) * ea.scaling).view(n, H, D)
+                cq = (ea.q_proj(h) * ea.scaling).view(n, H, D)
             c = ops.cross_attention(cq, st.cross_kv[:n, l, 0], st.cross_kv[:n, l, 1], st.cross_lens[:n], scale=1.0,
                                     workspace=st.cross_ws[n])
-            x = x + ea.out_proj(c.view(n, -1))
-            h = layer.final_layer_norm(x)
-            x = x + layer.fc2(layer.activation_fn(layer.fc1(h)))
-        logits = self.hf_model.proj_out(dec.layer_norm(x))
+            x, h = ops.add_layernorm(x, ea.out_proj(c.view(n, -1)), layer.final_layer_norm)
+            nxt = layers[l + 1].self_attn_layer_norm if l + 1 < len(layers) else dec.layer_norm
+            x, h = ops.add_layernorm(x, layer.fc2(layer.activation_fn(layer.fc1(h))), nxt)
+        logits = F.linear(h, _padded_head(self, self.hf_model.proj_out))[:, : self.vocab_size]
         if self.suppress_mask is not None:
             logits = logits.masked_fill(self.suppress_mask, float("-inf"))
         return torch.argmax(logits, dim=-1)

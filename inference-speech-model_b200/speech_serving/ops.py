@@ -327,3 +327,23 @@ def cross_kv_project(
         out.stride(0), dtype_code(enc_out.dtype), _ptr(error_word), _stream_handle())
     N.check(rc, "spd_cross_kv_project")
     return out
+
+
+# ----------------------------------------------------------------------------- decoder-layer glue
+def add_layernorm(x: torch.Tensor, delta: Optional[torch.Tensor], ln, out_y: Optional[torch.Tensor] = None):
+    """``x += delta`` (in place, rounded to x's dtype) and ``LayerNorm(x)`` in one kernel;
+    ``ln`` is an ``nn.LayerNorm`` over the last dimension.  Returns (x, y).  With
+    ``delta`` None only y = LayerNorm(x) is computed."""
+    _require_cuda("add_layernorm", x, delta)
+    cols = x.shape[-1]
+    if not x.is_contiguous() or (delta is not None and (delta.shape != x.shape or not delta.is_contiguous())):
+        raise RuntimeError("add_layernorm: x and delta must be contiguous and of one shape")
+    w, b = ln.weight, ln.bias
+    if w is None or b is None or w.dtype != x.dtype or b.dtype != x.dtype or (delta is not None and delta.dtype != x.dtype):
+        raise RuntimeError("add_layernorm: one dtype for x, delta and the LayerNorm's weight and bias")
+    y = torch.empty_like(x) if out_y is None else out_y
+    rc = N.load().spd_add_layernorm(x.data_ptr(), _ptr(delta), w.data_ptr(), b.data_ptr(),
+                                    x.data_ptr() if delta is not None else None, y.data_ptr(), x.numel() // cols, cols,
+                                    float(ln.eps), dtype_code(x.dtype), _stream_handle())
+    N.check(rc, "spd_add_layernorm")
+    return x, y

@@ -351,3 +351,26 @@ def test_block_gather_into_slot_layout_and_padding():
     ref = O.block_gather(pool.cpu().numpy(), tab, lens, T)
     assert np.array_equal(view.cpu().numpy(), ref)
     assert torch.all(slots[:, 0] == 7.0) and torch.all(slots[:, 1, 1] == 7.0)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("cols", [384, 768, 1280])
+def test_add_layernorm_matches_add_then_layernorm(dtype, cols):
+    """The fused residual add + LayerNorm: x_out is exactly the rounded sum, y matches
+    torch's LayerNorm of it (one output rounding apart)."""
+    torch.manual_seed(cols)
+    rows = 37
+    ln = torch.nn.LayerNorm(cols).to(DEV, dtype)
+    with torch.no_grad():
+        ln.weight.uniform_(0.5, 1.5)
+        ln.bias.uniform_(-0.5, 0.5)
+    x = torch.randn(rows, cols, device=DEV).to(dtype)
+    d = torch.randn(rows, cols, device=DEV).to(dtype)
+    ref_x = x + d
+    ref_y = torch.nn.functional.layer_norm(ref_x.float(), (cols,), ln.weight.float(), ln.bias.float(), ln.eps)
+    xo, y = ops.add_layernorm(x.clone(), d, ln)
+    assert torch.equal(xo, ref_x)
+    tol = {torch.float32: 1e-5, torch.float16: 4e-3, torch.bfloat16: 2e-2}[dtype]
+    torch.testing.assert_close(y.float(), ref_y, atol=tol, rtol=0)
+    _, y2 = ops.add_layernorm(ref_x.clone(), None, ln)
+    torch.testing.assert_close(y2.float(), ref_y, atol=tol, rtol=0)
