@@ -296,8 +296,11 @@ class PretrainedWhisperModel(nn.Module):
         super().__init__()
         self.device, self.dtype_ = device, dtype
         if config is not None:
+            # random weights drawn on the target device (seeded): large-v3 is 1.5 B
+            # parameters, slow to initialise on the host with several ranks at once
             torch.manual_seed(seed)
-            hf = WhisperForConditionalGeneration(config)
+            with torch.device(device):
+                hf = WhisperForConditionalGeneration(config)
         else:
             hf = WhisperForConditionalGeneration.from_pretrained(model_name_or_path, dtype=dtype,
                                                                  local_files_only=local_files_only)
