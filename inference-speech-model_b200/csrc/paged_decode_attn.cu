@@ -12,15 +12,15 @@
 // * A unit is one pool block of ALL heads: in the pool layout
 //   [num_blocks][block_size][H][D] that is one contiguous run of block_size*H*D
 //   elements, fetched with two 1-D bulk async copies (K and V; only the valid rows of a
-//   sequence's last block).  A work item is up to kItemUnits consecutive units of one
-//   sequence.
-// * Items are handed out dynamically: the producer warp of each CTA of a persistent
-//   grid takes the next item from a global atomic counter (prefetching one take ahead),
-//   so CTAs whose data arrives early simply do more items and the kernel ends when the
-//   item queue drains — the DRAM service order cannot leave stragglers.  The counter is
-//   reset by the last CTA to finish taking.
-// * Set-up is one parallel round trip: the context lengths and the whole block table
-//   come in by bulk copy (when they fit), while the first item is taken.
+//   sequence's last block) under an L2 evict-first policy.  A work item is chunk c of a
+//   sequence: its units [c*kItemUnits, (c+1)*kItemUnits).
+// * CTA g of the persistent grid starts on chunk g / B of sequence g % B: its producer
+//   reads that sequence's length and block ids with plain loads, so the first copies go
+//   out one round trip after the grid starts.  The lengths and the whole block table
+//   (when it fits) arrive by bulk copy meanwhile; every other chunk is queued
+//   (sequence-major) and handed out by a global atomic counter, one take ahead, so CTAs
+//   whose data arrives early simply do more items and the kernel ends when the queue
+//   drains.  The counter is reset by the last CTA to finish taking.
 // * The producer streams units through an S-stage shared-memory ring (full mbarriers
 //   complete on the copies' bytes, empty mbarriers collect one arrival per compute warp);
 //   per-stage metadata says which sequence/block/item a stage holds; a stage with
@@ -29,12 +29,12 @@
 // * Compute warp w owns heads [w*HPW, (w+1)*HPW) and never synchronises with the other
 //   compute warps: it patches its own slice of an appended row; at the end of an item it
 //   writes the output (an item covering the whole sequence) or a partial (m, l, acc) to
-//   slot [item][h].
+//   slot [b * chunks_per_sequence + c][h].
 // * Split sequences are merged by a second, small kernel (one warp per (sequence, head))
 //   launched with programmatic dependent launch: the streaming kernel signals
 //   launch_dependents at its start, so the merge kernel's CTAs are already resident, have
-//   located their items, and wait (griddepcontrol.wait) when the streaming kernel ends;
-//   then one round of loads brings in every partial of the sequence.
+//   read their sequence's length, and wait (griddepcontrol.wait) when the streaming
+//   kernel ends; then one round of loads brings in every partial of the sequence.
 // * q·k: 32/block_size lanes per row, q in registers (each score scaled by scale*log2 e), K
 //   chunks read in a per-row rotated order so the 8 lanes of a shared-memory phase hit
 //   distinct banks.  p·v: each lane owns one 16-byte chunk of a row.  Online softmax in
@@ -115,16 +115,21 @@ struct PagedGeom {
   static_assert((NCH & (NCH - 1)) == 0 && DPL % 2 == 0, "chunking");
 };
 
-// Per-stage metadata written by the producer before it arms the stage.
+// Per-stage metadata written by the producer before it arms the stage (two 16-byte words).
 struct StageMeta {
-  int b;      // sequence, or -1: no more work
-  int j;      // block index within the sequence
-  int item;   // global item index
-  int flags;  // kFirst | kLast
+  int b;        // sequence, or -1: no more work
+  int nvalid;   // valid rows of this unit
+  int slot;     // the item's partial slot: b * chunks_per_sequence + chunk
+  int flags;    // kFirst | kLast | kAppend
+  int phys;     // pool block of this unit
+  int nchunks;  // items (chunks) of sequence b
+  int pad0, pad1;
 };
-constexpr int kFirst = 1, kLast = 2;
+constexpr int kFirst = 1, kLast = 2, kAppend = 4;
 constexpr int kPairThreads = 416;  // two-CTA form: up to 12 compute warps + the producer
 constexpr int kPairMinSeqs = 128;  // batches at least this large use the two-CTA form
+
+__device__ __forceinline__ int clamp_ctx(int c, int max_ctx) { return c > max_ctx ? max_ctx : (c > 0 ? c : 0); }
 
 // PAIR: the two-CTAs-per-SM form (at most 12 compute warps, registers capped for two
 // resident CTAs, compact stages: the append rows are copied into the staged block).
@@ -139,10 +144,12 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
   const int H = p.H, B = p.B, S = p.stages, MB = p.max_blocks;
   const int HD = H * D;
   const int NW = (H + HPW - 1) / HPW;  // compute warps; warp NW is the producer
+  const int G = (int)gridDim.x;
+  const int MC = (MB + kItemUnits - 1) / kItemUnits;  // chunks (items) of a sequence at most
   const size_t unit_elems = (size_t)BS * HD;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-  // ---- shared memory: ring | barriers | metadata | lengths | item prefix | table ----
+  // ---- shared memory: ring | barriers | metadata | lengths | chunk prefix | table ----
   // K, V, q (and, in the single-CTA form, k_new / v_new rows for the fused append)
   const size_t stage_elems = 2 * unit_elems + (PAIR ? 1 : 3) * (size_t)HD;
   T* ring = reinterpret_cast<T*>(smem);
@@ -152,11 +159,11 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
   StageMeta* meta = reinterpret_cast<StageMeta*>(setup + 2);  // 16-byte aligned
   int* flag = reinterpret_cast<int*>(meta + S);               // [0] abort, [1..3] spare
   int* ctx_s = flag + 4;                                      // [round4(B)] context lengths
-  int* ip = ctx_s + ((B + 3) & ~3);                           // [B + 1] item prefix
+  int* ip = ctx_s + ((B + 3) & ~3);                           // [B + 1] queued-chunk prefix
   int* tab_s = ip + ((B + 4) & ~3);                           // [B * MB] block table copy
   const bool tab_in_smem = p.table_in_smem != 0;
 
-  int* next_item = p.work + 0;  // global item counter
+  int* next_item = p.work + 0;  // queue counter
   int* done_ctas = p.work + 1;  // CTAs that finished taking items
   const T* __restrict__ kpool = reinterpret_cast<const T*>(p.k_pool);
   const T* __restrict__ vpool = reinterpret_cast<const T*>(p.v_pool);
@@ -166,15 +173,8 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
   const int max_ctx = MB * BS;
 
   if (tid == 0) SPD_TRACE(0);
-  // ---- 1. set-up: barriers, bulk copies of lengths and table, first item take ------
-  const bool ctx_bulk = ((B * 4) % 16 == 0) && ((reinterpret_cast<uintptr_t>(p.context_lens) & 15) == 0);
+  // ---- 1. shared-memory set-up, while the previous kernel in the stream may still run --
   if (tid < 4) flag[tid] = 0;  // shared memory starts undefined
-  // Launched with programmatic dependent launch: this grid may become resident while the
-  // previous kernel in the stream still runs, so every thread waits for it before reading
-  // an input or writing an output.  Then the merge kernel that follows may get resident
-  // early; it waits for this grid to finish (griddepcontrol.wait) before reading anything.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -182,137 +182,175 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
     }
     mbar_init(setup, 1);
     fence_barrier_init();
-    const uint32_t tx = (ctx_bulk ? (uint32_t)B * 4u : 0u) + (tab_in_smem ? (uint32_t)B * MB * 4u : 0u);
-    if (tx) {
-      mbar_arrive_expect_tx(setup, tx);
-      if (ctx_bulk) bulk_copy_g2s(ctx_s, p.context_lens, (uint32_t)B * 4u, setup);
-      if (tab_in_smem) bulk_copy_g2s(tab_s, p.block_tables, (uint32_t)B * MB * 4u, setup);
-    } else {
-      mbar_arrive(setup);
-    }
   }
   __syncthreads();
-  if (!mbar_wait_bounded(setup, 0, p.err)) flag[0] = 1;
-  if (!ctx_bulk) {
-    for (int i = tid; i < B; i += blockDim.x) ctx_s[i] = p.context_lens[i];
-  }
-  __syncthreads();
-  // clamp lengths, items per sequence, and their prefix (warp 0 scans)
-  if (warp == 0) {
-    int carry = 0;
-    for (int base = 0; base < B; base += 32) {
-      const int i = base + lane;
-      int v = 0;
-      if (i < B) {
-        int c = ctx_s[i];
-        if (c > max_ctx) {
-          set_error(p.err, SPD_DEVERR_LENGTH);
-          c = max_ctx;
-        }
-        c = c > 0 ? c : 0;
-        ctx_s[i] = c;
-        const int nblk = (c + BS - 1) / BS;
-        v = (nblk + kItemUnits - 1) / kItemUnits;
-      }
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += n;
-      }
-      if (i < B) ip[i + 1] = v + carry;
-      carry += __shfl_sync(0xffffffffu, v, 31);
-    }
-    if (lane == 0) ip[0] = 0;
-  }
-  __syncthreads();
-  if (tid == 0) SPD_TRACE(1);
-  const int n_items = ip[B];
-
-  // sequences with nothing to attend to get zeros (CTA b % gridDim, compute threads)
-  for (int b = blockIdx.x; b < B; b += gridDim.x) {
-    if (ctx_s[b] == 0) {
-      for (int i = tid; i < HD; i += blockDim.x) out[(size_t)b * HD + i] = Elem<T>::from_f(0.f);
-    }
-  }
+  // Launched with programmatic dependent launch: this grid may become resident while the
+  // previous kernel in the stream still runs, so every thread waits for it before reading
+  // an input or writing an output.  Then the merge kernel that follows may get resident
+  // early; it waits for this grid to finish (griddepcontrol.wait) before reading anything.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (tid == 0) SPD_TRACE(6);
 
   // ---- 2. producer warp --------------------------------------------------------------
+  // Work: chunk c of sequence b (blocks [c*kItemUnits, (c+1)*kItemUnits)) is one item.
+  // CTA g starts on chunk g / B of sequence g % B, located with direct loads so that its
+  // copies start one round trip after the wait; the other chunks form a queue (sequence-
+  // major) handed out by a global counter once the lengths have arrived.
   if (warp == NW) {
-    if (lane == 0) {
-      int s = 0;
-      uint32_t ph = 0;
-      long long n_issued = 0;
-      bool alive = !flag[0];
-      // The first item of CTA c is c; later items come from the shared counter, offset by
-      // the grid size (no contended atomic before the first copy is issued).
-      int item = blockIdx.x;
-      while (alive && item < n_items) {
-        const int nxt = (int)gridDim.x + atomicAdd(next_item, 1);  // next take, in flight meanwhile
-        const int b = upper_index_i32(ip, B, item);
-        const int nblk = (ctx_s[b] + BS - 1) / BS;
-        const int j0 = (item - ip[b]) * kItemUnits;
-        const int j1 = min(j0 + kItemUnits, nblk);
-        for (int j = j0; j < j1; ++j) {
-          if (n_issued >= S && (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&empty[s], ph ^ 1, p.err))) {
-            flag[0] = 1;
-            alive = false;
-            break;
-          }
-          const int nvalid = min(BS, ctx_s[b] - j * BS);
-          int phys = tab_in_smem ? tab_s[b * MB + j] : p.block_tables[(size_t)b * MB + j];
-          if (phys < 0 || phys >= p.num_blocks) {
-            set_error(p.err, SPD_DEVERR_BLOCK_ID);
-            phys = 0;
-          }
-          const bool first = (j == j0), last = (j == j1 - 1);
-          const bool app = append && (j == nblk - 1);
-          meta[s] = StageMeta{b, j, item, (first ? kFirst : 0) | (last ? kLast : 0)};
-          const size_t off = (size_t)phys * unit_elems;
-          const uint32_t row_bytes = (uint32_t)(HD * (int)sizeof(T));
-          T* dst = ring + (size_t)s * stage_elems;
-          if constexpr (PAIR) {
-            // compact stages: the new row (nvalid-1) comes from k_new / v_new straight into
-            // its place, the pool supplies the rows before it
-            const int npool = app ? nvalid - 1 : nvalid;
-            const uint32_t bytes = (uint32_t)npool * row_bytes;
-            mbar_arrive_expect_tx(&full[s], 2 * bytes + (first ? row_bytes : 0u) + (app ? 2 * row_bytes : 0u));
-            if (npool > 0) {
-              bulk_copy_g2s(dst, kpool + off, bytes, &full[s]);
-              bulk_copy_g2s(dst + unit_elems, vpool + off, bytes, &full[s]);
-            }
-            if (first) bulk_copy_g2s(dst + 2 * unit_elems, qg + (size_t)b * HD, row_bytes, &full[s]);
-            if (app) {
-              bulk_copy_g2s(dst + (size_t)(nvalid - 1) * HD, reinterpret_cast<const T*>(p.k_new) + (size_t)b * HD,
-                            row_bytes, &full[s]);
-              bulk_copy_g2s(dst + unit_elems + (size_t)(nvalid - 1) * HD,
-                            reinterpret_cast<const T*>(p.v_new) + (size_t)b * HD, row_bytes, &full[s]);
-            }
-          } else {
-            const uint32_t bytes = (uint32_t)(nvalid * HD * (int)sizeof(T));
-            mbar_arrive_expect_tx(&full[s], 2 * bytes + (first ? row_bytes : 0u) + (app ? 2 * row_bytes : 0u));
-            bulk_copy_g2s(dst, kpool + off, bytes, &full[s]);
-            bulk_copy_g2s(dst + unit_elems, vpool + off, bytes, &full[s]);
-            if (first) bulk_copy_g2s(dst + 2 * unit_elems, qg + (size_t)b * HD, row_bytes, &full[s]);
-            if (app) {
-              bulk_copy_g2s(dst + 2 * unit_elems + HD, reinterpret_cast<const T*>(p.k_new) + (size_t)b * HD,
-                            row_bytes, &full[s]);
-              bulk_copy_g2s(dst + 2 * unit_elems + 2 * HD, reinterpret_cast<const T*>(p.v_new) + (size_t)b * HD,
-                            row_bytes, &full[s]);
-            }
-          }
-          if (n_issued == 0) SPD_TRACE(2);
-          ++n_issued;
-          if (++s == S) {
-            s = 0;
-            ph ^= 1;
-          }
+    const uint64_t pol = l2_policy_evict_first();
+    int s = 0;
+    uint32_t ph = 0;
+    long long n_issued = 0;
+    bool alive = true;
+    const uint32_t row_bytes = (uint32_t)(HD * (int)sizeof(T));
+    // stages the unit j of item (b, chunk) (lane 0 only)
+    auto issue_unit = [&](int b, int j, int ctx, int phys, int chunk, int nch, bool first, bool last) {
+      if (n_issued >= S && (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&empty[s], ph ^ 1, p.err))) {
+        flag[0] = 1;
+        alive = false;
+        return;
+      }
+      const int nblk = (ctx + BS - 1) / BS;
+      const int nvalid = min(BS, ctx - j * BS);
+      if (phys < 0 || phys >= p.num_blocks) {
+        set_error(p.err, SPD_DEVERR_BLOCK_ID);
+        phys = 0;
+      }
+      const bool app = append && (j == nblk - 1);
+      meta[s] = StageMeta{b, nvalid, b * MC + chunk, (first ? kFirst : 0) | (last ? kLast : 0) | (app ? kAppend : 0),
+                          phys, nch, 0, 0};
+      const size_t off = (size_t)phys * unit_elems;
+      T* dst = ring + (size_t)s * stage_elems;
+      if constexpr (PAIR) {
+        // compact stages: the new row (nvalid-1) comes from k_new / v_new straight into
+        // its place, the pool supplies the rows before it
+        const int npool = app ? nvalid - 1 : nvalid;
+        const uint32_t bytes = (uint32_t)npool * row_bytes;
+        mbar_arrive_expect_tx(&full[s], 2 * bytes + (first ? row_bytes : 0u) + (app ? 2 * row_bytes : 0u));
+        if (npool > 0) {
+          bulk_copy_g2s_hint(dst, kpool + off, bytes, &full[s], pol);
+          bulk_copy_g2s_hint(dst + unit_elems, vpool + off, bytes, &full[s], pol);
         }
-        item = nxt;
+        if (first) bulk_copy_g2s(dst + 2 * unit_elems, qg + (size_t)b * HD, row_bytes, &full[s]);
+        if (app) {
+          bulk_copy_g2s(dst + (size_t)(nvalid - 1) * HD, reinterpret_cast<const T*>(p.k_new) + (size_t)b * HD,
+                        row_bytes, &full[s]);
+          bulk_copy_g2s(dst + unit_elems + (size_t)(nvalid - 1) * HD,
+                        reinterpret_cast<const T*>(p.v_new) + (size_t)b * HD, row_bytes, &full[s]);
+        }
+      } else {
+        const uint32_t bytes = (uint32_t)nvalid * row_bytes;
+        mbar_arrive_expect_tx(&full[s], 2 * bytes + (first ? row_bytes : 0u) + (app ? 2 * row_bytes : 0u));
+        bulk_copy_g2s_hint(dst, kpool + off, bytes, &full[s], pol);
+        bulk_copy_g2s_hint(dst + unit_elems, vpool + off, bytes, &full[s], pol);
+        if (first) bulk_copy_g2s(dst + 2 * unit_elems, qg + (size_t)b * HD, row_bytes, &full[s]);
+        if (app) {
+          bulk_copy_g2s(dst + 2 * unit_elems + HD, reinterpret_cast<const T*>(p.k_new) + (size_t)b * HD, row_bytes,
+                        &full[s]);
+          bulk_copy_g2s(dst + 2 * unit_elems + 2 * HD, reinterpret_cast<const T*>(p.v_new) + (size_t)b * HD,
+                        row_bytes, &full[s]);
+        }
+      }
+      if (n_issued == 0) SPD_TRACE(2);
+      ++n_issued;
+      if (++s == S) {
+        s = 0;
+        ph ^= 1;
+      }
+    };
+    const bool ctx_bulk = ((B * 4) % 16 == 0) && ((reinterpret_cast<uintptr_t>(p.context_lens) & 15) == 0);
+    int q = 0;
+    if (lane == 0) {
+      // lengths and table into shared memory, overlapping the first item's loads
+      const uint32_t tx = (ctx_bulk ? (uint32_t)B * 4u : 0u) + (tab_in_smem ? (uint32_t)B * MB * 4u : 0u);
+      if (tx) {
+        mbar_arrive_expect_tx(setup, tx);
+        if (ctx_bulk) bulk_copy_g2s(ctx_s, p.context_lens, (uint32_t)B * 4u, setup);
+        if (tab_in_smem) bulk_copy_g2s(tab_s, p.block_tables, (uint32_t)B * MB * 4u, setup);
+      } else {
+        mbar_arrive(setup);
+      }
+      const int b0 = (int)blockIdx.x % B, c0 = (int)blockIdx.x / B;
+      if (c0 < MC) {
+        const int ctx0 = clamp_ctx(p.context_lens[b0], max_ctx);
+        int ph0[kItemUnits];
+#pragma unroll
+        for (int u = 0; u < kItemUnits; ++u) {
+          const int j = c0 * kItemUnits + u;
+          ph0[u] = j < MB ? p.block_tables[(size_t)b0 * MB + j] : 0;
+        }
+        const int nblk0 = (ctx0 + BS - 1) / BS;
+        const int nch0 = (nblk0 + kItemUnits - 1) / kItemUnits;
+        if (c0 < nch0) {
+          const int j0 = c0 * kItemUnits, j1 = min(j0 + kItemUnits, nblk0);
+#pragma unroll
+          for (int u = 0; u < kItemUnits; ++u)
+            if (j0 + u < j1 && alive) issue_unit(b0, j0 + u, ctx0, ph0[u], c0, nch0, u == 0, j0 + u == j1 - 1);
+        }
+      }
+      q = atomicAdd(next_item, 1);  // first queue take, in flight during the scan
+    }
+    __syncwarp();
+    // lengths: clamp, chunks per sequence, and the prefix of each sequence's queued chunks
+    // (its chunks minus the ones CTAs started on)
+    if (!mbar_wait_bounded(setup, 0, p.err)) flag[0] = 1;
+    if (!ctx_bulk)
+      for (int i = lane; i < B; i += 32) ctx_s[i] = p.context_lens[i];
+    __syncwarp();
+    {
+      int carry = 0;
+      for (int base = 0; base < B; base += 32) {
+        const int i = base + lane;
+        int v = 0;
+        if (i < B) {
+          const int c0 = ctx_s[i];
+          if (c0 > max_ctx) set_error(p.err, SPD_DEVERR_LENGTH);
+          const int c = clamp_ctx(c0, max_ctx);
+          ctx_s[i] = c;
+          const int nch = ((c + BS - 1) / BS + kItemUnits - 1) / kItemUnits;
+          const int started = i < G ? min((G - 1 - i) / B + 1, nch) : 0;
+          v = nch - started;
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int n = __shfl_up_sync(0xffffffffu, v, o);
+          if (lane >= o) v += n;
+        }
+        if (i < B) ip[i + 1] = v + carry;
+        carry += __shfl_sync(0xffffffffu, v, 31);
+      }
+      if (lane == 0) ip[0] = 0;
+    }
+    __syncwarp();
+    if (lane == 0) SPD_TRACE(1);
+    // sequences with nothing to attend to get zeros (sequence b by CTA b % G)
+    for (int b = blockIdx.x; b < B; b += G)
+      if (ctx_s[b] == 0)
+        for (int i = lane; i < HD; i += 32) out[(size_t)b * HD + i] = Elem<T>::from_f(0.f);
+    if (lane == 0) {
+      const int n_queue = ip[B];
+      alive = alive && !flag[0];
+      while (alive && q < n_queue) {
+        const int nxt = atomicAdd(next_item, 1);  // next take, in flight meanwhile
+        const int b = upper_index_i32(ip, B, q);
+        const int ctx = ctx_s[b];
+        const int nblk = (ctx + BS - 1) / BS;
+        const int nch = (nblk + kItemUnits - 1) / kItemUnits;
+        const int started = b < G ? min((G - 1 - b) / B + 1, nch) : 0;
+        const int c = started + (q - ip[b]);
+        const int j0 = c * kItemUnits, j1 = min(j0 + kItemUnits, nblk);
+        for (int j = j0; j < j1 && alive; ++j) {
+          const int phys = tab_in_smem ? tab_s[b * MB + j] : p.block_tables[(size_t)b * MB + j];
+          issue_unit(b, j, ctx, phys, c, nch, j == j0, j == j1 - 1);
+        }
+        q = nxt;
       }
       SPD_TRACE(3);
       // end-of-work stage for the compute warps
       if (alive && n_issued >= S && !mbar_wait_bounded(&empty[s], ph ^ 1, p.err)) alive = false;
       if (alive) {
-        meta[s] = StageMeta{-1, 0, 0, 0};
+        meta[s] = StageMeta{-1, 0, 0, 0, 0, 0, 0, 0};
         mbar_arrive(&full[s]);
       } else {
         flag[0] = 1;
@@ -320,7 +358,7 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
       // This CTA takes no more items; the last CTA to get here re-arms the counter for
       // the next launch (every CTA's final take has already happened).
       __threadfence();
-      if (atomicAdd(done_ctas, 1) == (int)gridDim.x - 1) {
+      if (atomicAdd(done_ctas, 1) == G - 1) {
         *((volatile int*)next_item) = 0;
         *((volatile int*)done_ctas) = 0;
         __threadfence();
@@ -361,8 +399,8 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
       SPD_TRACE(4);
       traced = true;
     }
-    const int b = mt.b, j = mt.j;
-    const int nvalid = min(BS, ctx_s[b] - j * BS);
+    const int b = mt.b;
+    const int nvalid = mt.nvalid;
     T* Ks = ring + (size_t)s * stage_elems;
     T* Vs = Ks + unit_elems;
     const T* Qs = Vs + unit_elems;
@@ -386,12 +424,10 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
       }
     }
 
-    const int nblk = (ctx_s[b] + BS - 1) / BS;
-    if (append && j == nblk - 1) {
+    if (mt.flags & kAppend) {
       // op (3) fused: the new token is row nvalid-1 of the last block; this warp writes
       // its own heads' slice into the stage (so its q·k sees it) and into the pool.
-      int phys = tab_in_smem ? tab_s[b * MB + j] : p.block_tables[(size_t)b * MB + j];
-      if (phys < 0 || phys >= p.num_blocks) phys = 0;  // flagged by the producer
+      const size_t blk = (size_t)mt.phys * unit_elems;
       const size_t row_off = (size_t)(nvalid - 1) * HD;
       constexpr int VEC = 16 / sizeof(T);
       for (int k = 0; k < HPW; ++k) {
@@ -400,17 +436,15 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
         for (int i = lane * VEC; i < D; i += 32 * VEC) {
           const size_t e = row_off + (size_t)h * D + i;
           if constexpr (PAIR) {  // the new row arrived in its place in the staged block
-            *reinterpret_cast<uint4*>(const_cast<T*>(kpool) + (size_t)phys * unit_elems + e) =
-                *reinterpret_cast<const uint4*>(Ks + e);
-            *reinterpret_cast<uint4*>(const_cast<T*>(vpool) + (size_t)phys * unit_elems + e) =
-                *reinterpret_cast<const uint4*>(Vs + e);
+            *reinterpret_cast<uint4*>(const_cast<T*>(kpool) + blk + e) = *reinterpret_cast<const uint4*>(Ks + e);
+            *reinterpret_cast<uint4*>(const_cast<T*>(vpool) + blk + e) = *reinterpret_cast<const uint4*>(Vs + e);
           } else {  // fill the new row's place in the staged block, and the pool
             const uint4 kv = *reinterpret_cast<const uint4*>(Qs + HD + h * D + i);
             const uint4 vv = *reinterpret_cast<const uint4*>(Qs + 2 * HD + h * D + i);
             *reinterpret_cast<uint4*>(Ks + e) = kv;
             *reinterpret_cast<uint4*>(Vs + e) = vv;
-            *reinterpret_cast<uint4*>(const_cast<T*>(kpool) + (size_t)phys * unit_elems + e) = kv;
-            *reinterpret_cast<uint4*>(const_cast<T*>(vpool) + (size_t)phys * unit_elems + e) = vv;
+            *reinterpret_cast<uint4*>(const_cast<T*>(kpool) + blk + e) = kv;
+            *reinterpret_cast<uint4*>(const_cast<T*>(vpool) + blk + e) = vv;
           }
         }
       }
@@ -481,7 +515,7 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
 
     if (!(mt.flags & kLast)) continue;
     // ---- item end: the output, or a partial for the merge kernel --------------------------
-    const int nitems = ip[b + 1] - ip[b];
+    const int nitems = mt.nchunks;
 #pragma unroll
     for (int k = 0; k < HPW; ++k) {
       const int h = warp * HPW + k;
@@ -506,7 +540,7 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
         }
         continue;
       }
-      float* slot = p.partials + ((size_t)mt.item * H + h) * (D + 2);
+      float* slot = p.partials + ((size_t)mt.slot * H + h) * (D + 2);
       if (rg == 0) {
 #pragma unroll
         for (int i = 0; i < VE / 2; ++i) *reinterpret_cast<float2*>(slot + cidx * VE + 2 * i) = acc[k][i];
@@ -522,12 +556,12 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
 
 // ------------------------------------------------------------------ merge kernel
 // One warp per (sequence, head) of a sequence that spans more than one item.  Launched
-// with programmatic dependent launch right behind the streaming kernel.  The lengths are
-// read, and the sequence's item range worked out, while the streaming kernel still runs:
-// the streaming kernel never writes them, and it triggers this launch only after its own
-// griddepcontrol.wait, so everything written before it is final.  After
-// griddepcontrol.wait every partial of the sequence is loaded in one round trip (lane =
-// item for (m, l); all items' acc before any of it is used).
+// with programmatic dependent launch right behind the streaming kernel.  The sequence's
+// length is read while the streaming kernel still runs: the streaming kernel never writes
+// it, and it triggers this launch only after its own griddepcontrol.wait, so everything
+// written before it is final.  The partials of sequence b sit at slots
+// [b * chunks_per_sequence, + its chunks); after griddepcontrol.wait all of them are
+// loaded in one round trip (lane = item for (m, l); all items' acc before any is used).
 template <typename T, int D, int BS>
 __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
   constexpr int DL = (D + 31) / 32;  // acc elements per lane
@@ -537,22 +571,13 @@ __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
   const bool live = pair < (long long)p.B * p.H;
   const int b = live ? (int)(pair / p.H) : 0, h = live ? (int)(pair % p.H) : 0;
   const int max_ctx = p.max_blocks * BS;
-  // sequence b's first item = sum over b' < b of ceil(ceil(ctx/BS)/kItemUnits)
-  int ctx_b = live ? p.context_lens[b] : 0;
-  ctx_b = ctx_b > max_ctx ? max_ctx : (ctx_b > 0 ? ctx_b : 0);
-  int i0 = 0;
-  for (int bb = lane; bb < b && live; bb += 32) {
-    int c = p.context_lens[bb];
-    c = c > max_ctx ? max_ctx : (c > 0 ? c : 0);
-    i0 += ((c + BS - 1) / BS + kItemUnits - 1) / kItemUnits;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) i0 += __shfl_xor_sync(0xffffffffu, i0, o);
+  const int MC = (p.max_blocks + kItemUnits - 1) / kItemUnits;
+  const int ctx_b = live ? clamp_ctx(p.context_lens[b], max_ctx) : 0;
   const int nitems = ((ctx_b + BS - 1) / BS + kItemUnits - 1) / kItemUnits;
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the streaming kernel has finished
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (!live || nitems <= 1) return;  // written by the streaming kernel (or zero)
-  const float* base = p.partials + ((size_t)i0 * p.H + h) * (D + 2);
+  const float* base = p.partials + ((size_t)b * MC * p.H + h) * (D + 2);
   const size_t stride = (size_t)p.H * (D + 2);  // next item, same head
   T* orow = reinterpret_cast<T*>(p.out) + ((size_t)b * p.H + h) * D;
   if (nitems <= MAXI) {
@@ -633,7 +658,7 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
                      (reinterpret_cast<uintptr_t>(p.block_tables) & 15) == 0)
                         ? 1
                         : 0;
-  const size_t fixed = 16 * 8 /*barriers*/ + 16 * 8 /*meta*/ + 16 + 4 * ((size_t)p.B + 4) * 2 +
+  const size_t fixed = 16 * 8 /*barriers*/ + 32 * 8 /*meta*/ + 16 + 4 * ((size_t)p.B + 4) * 2 +
                        (p.table_in_smem ? tab_bytes : 0) + 256;
   // Ring depth: up to ~216 KB per CTA (one CTA per SM at the Whisper shapes; the
   // producer warp keeps every stage in flight), at least two stages.
@@ -642,7 +667,7 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
   if (S < 2 && 2 * stage_bytes + fixed <= 227 * 1024) S = 2;
   S = S < 1 ? 1 : (S > 8 ? 8 : S);
   p.stages = S;
-  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * ((size_t)S * 2 + 2) + 16 * (size_t)S + 16 +
+  const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * ((size_t)S * 2 + 2) + 32 * (size_t)S + 16 +
                       4 * ((((size_t)p.B + 3) & ~(size_t)3) + (((size_t)p.B + 4) & ~(size_t)3)) +
                       (p.table_in_smem ? tab_bytes : 0);
   if (smem > (PAIR ? 113 : 227) * 1024) return SPD_ERR_UNSUPPORTED;

@@ -140,6 +140,25 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 
 // 1-D bulk async copy global -> shared (no multicast).  dst, src 16-byte aligned,
 // bytes a multiple of 16.  Completion is signalled as transaction bytes on `bar`.
+// L2 policy for data read once per launch (the K/V stream): its lines are the first to
+// be evicted, so the small inputs, partials and code that the next launch reads again
+// stay resident in L2.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// As bulk_copy_g2s, with an L2 cache policy for the source lines.
+__device__ __forceinline__ void bulk_copy_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                   uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+      "%4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
                                               uint64_t* bar) {
   asm volatile(
