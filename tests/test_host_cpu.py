@@ -216,3 +216,39 @@ def test_pretrained_whisper_prefill_matches_hf_decoder():
         ref2 = hf.proj_out(hf.model.decoder(input_ids=ids2, encoder_hidden_states=e).last_hidden_state)
         torch.testing.assert_close(o2.logits[:, -1], ref2[:, -1], atol=1e-5, rtol=1e-5)
     assert [l.keys.shape[2] for l in o2.past_key_values.layers] == [5, 5]
+
+
+def test_hf_attention_patch_swaps_and_restores_forwards():
+    """patch_decoder replaces self_attn / encoder_attn forwards of every decoder layer and
+    the handle puts the originals back (reference: scripts/evaluate_paging_variants.py:
+    613-646 and its restore loop); a bad state is refused on the host."""
+    from transformers import WhisperConfig, WhisperForConditionalGeneration
+
+    from speech_serving.hf_attention import PagedDecodeState, patch_decoder
+
+    cfg = WhisperConfig(vocab_size=100, num_mel_bins=80, encoder_layers=1, decoder_layers=2, d_model=64,
+                        encoder_attention_heads=2, decoder_attention_heads=2, encoder_ffn_dim=128,
+                        decoder_ffn_dim=128, max_source_positions=16, max_target_positions=32, pad_token_id=0,
+                        bos_token_id=1, eos_token_id=1, decoder_start_token_id=2)
+    dec = WhisperForConditionalGeneration(cfg).model.decoder
+    pools = [torch.zeros(4, 16, 2, 32) for _ in range(2)]
+    tables, lens = torch.zeros(3, 2, dtype=torch.int32), torch.zeros(3, dtype=torch.int32)
+    ck = [torch.zeros(3, 2, 16, 32) for _ in range(2)]
+    state = PagedDecodeState(pools, pools, tables, lens, cross_k=ck, cross_v=ck,
+                             cross_lens=torch.full((3,), 16, dtype=torch.int32))
+    before = [(lay.self_attn.forward, lay.encoder_attn.forward) for lay in dec.layers]
+    handle = patch_decoder(dec, state)
+    assert all(lay.self_attn.forward != b[0] and lay.encoder_attn.forward != b[1]
+               for lay, b in zip(dec.layers, before))
+    with pytest.raises(RuntimeError):  # one new token per sequence
+        dec.layers[0].self_attn(torch.zeros(3, 2, 64))
+    handle.restore()
+    assert [(lay.self_attn.forward, lay.encoder_attn.forward) for lay in dec.layers] == before
+    state.advance(2)
+    assert state.context_lens.tolist() == [2, 2, 2]
+    with pytest.raises(ValueError):
+        PagedDecodeState(pools, pools, tables.long(), lens)
+    with pytest.raises(ValueError):
+        patch_decoder(dec, PagedDecodeState(pools[:1], pools[:1], tables, lens), cross=False)
+    with pytest.raises(ValueError):
+        patch_decoder(dec, PagedDecodeState(pools, pools, tables, lens), cross=True)
