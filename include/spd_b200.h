@@ -175,7 +175,7 @@ int spd_add_layernorm(const void* x, const void* delta, const void* gamma, const
  *   split-KV scratch lives in a 4 MiB array inside the library that every GPU using this
  *   entry point keeps until the process exits (SPD_NOALLOC_SCRATCH_BYTES).  Calls whose
  *   spd_paged_decode_attn_workspace_size(B, H, D, device) exceeds it are rejected with
- *   SPD_ERR_WORKSPACE (e.g. B=64, H=12, D=64, 28 blocks per table needs about 2.9 MiB).
+ *   SPD_ERR_WORKSPACE (e.g. B=64, H=12, D=64, 28 blocks per table needs about 3.0 MiB).
  *   error_word: optional int32 device word that receives this call's SPD_DEVERR_* flags.
  *   The first call on each device looks up the array's device address; make that first
  *   call before capturing any stream.  Every call clears the scratch counters it needs,

@@ -131,6 +131,11 @@ constexpr int kPairMinSeqs = 128;  // batches at least this large use the two-CT
 
 __device__ __forceinline__ int clamp_ctx(int c, int max_ctx) { return c > max_ctx ? max_ctx : (c > 0 ? c : 0); }
 
+// floats per split partial row (acc[D], m, l, zeros): a whole number of 32-byte sectors
+template <int D>
+constexpr int kPartialRow = D + 8;
+static_assert(kPartialRow<16> % 8 == 0 && kPartialRow<128> % 8 == 0, "sector-aligned partial rows");
+
 // PAIR: the two-CTAs-per-SM form (at most 12 compute warps, registers capped for two
 // resident CTAs, compact stages: the append rows are copied into the staged block).
 template <typename T, int D, int BS, int HPW, bool PAIR>
@@ -540,14 +545,17 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
         }
         continue;
       }
-      float* slot = p.partials + ((size_t)mt.slot * H + h) * (D + 2);
+      // a partial row: acc[D], then (m, l) and zeros filling the last 32-byte sector; kept
+      // in L2 for the merge kernel
+      float* slot = p.partials + ((size_t)mt.slot * H + h) * kPartialRow<D>;
+      const uint64_t keep = l2_policy_evict_last();
       if (rg == 0) {
 #pragma unroll
-        for (int i = 0; i < VE / 2; ++i) *reinterpret_cast<float2*>(slot + cidx * VE + 2 * i) = acc[k][i];
+        for (int i = 0; i < VE / 2; ++i) st_global_hint(slot + cidx * VE + 2 * i, acc[k][i], keep);
       }
       if (lane == 0) {
-        slot[D] = m[k];
-        slot[D + 1] = ltot;
+        st_global_hint(slot + D, make_float4(m[k], ltot, 0.f, 0.f), keep);
+        st_global_hint(slot + D + 4, make_float4(0.f, 0.f, 0.f, 0.f), keep);
       }
     }
   }
@@ -564,8 +572,11 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
 // loaded in one round trip (lane = item for (m, l); all items' acc before any is used).
 template <typename T, int D, int BS>
 __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
-  constexpr int DL = (D + 31) / 32;  // acc elements per lane
-  constexpr int MAXI = 32;           // items per sequence held in registers
+  constexpr int DL = (D + 31) / 32;             // acc elements per lane (two-pass path)
+  constexpr int EPL = D >= 64 ? D / 32 : 2;      // acc elements per lane (register path)
+  using V = std::conditional_t<EPL == 4, float4, float2>;
+  static_assert(EPL == 2 || EPL == 4, "head_dim");
+  constexpr int MAXI = 16;  // items per sequence held in registers (a 448-token context has 14)
   const int lane = threadIdx.x & 31;
   const long long pair = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const bool live = pair < (long long)p.B * p.H;
@@ -577,37 +588,40 @@ __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the streaming kernel has finished
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (!live || nitems <= 1) return;  // written by the streaming kernel (or zero)
-  const float* base = p.partials + ((size_t)b * MC * p.H + h) * (D + 2);
-  const size_t stride = (size_t)p.H * (D + 2);  // next item, same head
+  const float* base = p.partials + ((size_t)b * MC * p.H + h) * kPartialRow<D>;
+  const size_t stride = (size_t)p.H * kPartialRow<D>;  // next item, same head
   T* orow = reinterpret_cast<T*>(p.out) + ((size_t)b * p.H + h) * D;
   if (nitems <= MAXI) {
+    // lane l holds elements [l*EPL, (l+1)*EPL) of every item's acc: one vector load per item
     float2 ml = make_float2(-INFINITY, 0.f);
-    float a[MAXI][DL];
     if (lane < nitems) ml = __ldcg(reinterpret_cast<const float2*>(base + lane * stride + D));
+    const bool hold = lane < D / EPL;
+    V a[MAXI];
 #pragma unroll
-    for (int it = 0; it < MAXI; ++it) {
-#pragma unroll
-      for (int e = 0; e < DL; ++e) {
-        const int d = lane + 32 * e;
-        a[it][e] = (it < nitems && d < D) ? __ldcg(base + it * stride + d) : 0.f;
-      }
-    }
+    for (int it = 0; it < MAXI; ++it)
+      a[it] = (it < nitems && hold) ? __ldcg(reinterpret_cast<const V*>(base + it * stride) + lane) : V{};
     const float M = warp_max(ml.x);
     const float w = lane < nitems ? exp2f(ml.x - M) : 0.f;
     const float inv = 1.f / warp_sum(ml.y * w);
-    float o[DL];
-#pragma unroll
-    for (int e = 0; e < DL; ++e) o[e] = 0.f;
+    V o{};
 #pragma unroll
     for (int it = 0; it < MAXI; ++it) {
       const float wi = __shfl_sync(0xffffffffu, w, it);
-#pragma unroll
-      for (int e = 0; e < DL; ++e) o[e] = fmaf(wi, a[it][e], o[e]);
+      o.x = fmaf(wi, a[it].x, o.x);
+      o.y = fmaf(wi, a[it].y, o.y);
+      if constexpr (EPL == 4) {
+        o.z = fmaf(wi, a[it].z, o.z);
+        o.w = fmaf(wi, a[it].w, o.w);
+      }
     }
-#pragma unroll
-    for (int e = 0; e < DL; ++e) {
-      const int d = lane + 32 * e;
-      if (d < D) orow[d] = Elem<T>::from_f(o[e] * inv);
+    if (hold) {
+      T* dst = orow + lane * EPL;
+      dst[0] = Elem<T>::from_f(o.x * inv);
+      dst[1] = Elem<T>::from_f(o.y * inv);
+      if constexpr (EPL == 4) {
+        dst[2] = Elem<T>::from_f(o.z * inv);
+        dst[3] = Elem<T>::from_f(o.w * inv);
+      }
     }
     return;
   }

@@ -96,7 +96,7 @@ size_t spd_paged_decode_attn_workspace_size(int B, int H, int D, int max_blocks,
   if (B <= 0 || H <= 0 || D <= 0 || max_blocks <= 0 || sm_count(device) <= 0) return 0;
   const size_t items = (size_t)B * ((max_blocks + spd::kItemUnits - 1) / spd::kItemUnits);
   return spd::kWsHeaderBytes + spd::round_up((size_t)B * H * 4, 256) +
-         spd::round_up(items * H * (D + 2) * 4, 256);
+         spd::round_up(items * H * (D + 8) * 4, 256);  // partial rows of D + 8 floats
 }
 
 size_t spd_cross_attn_workspace_size(int B, int H, int D, int device) {

@@ -149,6 +149,24 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   return pol;
 }
 
+// L2 policy for data the next kernel reads back (split partials): kept over the stream.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// 8- and 16-byte global stores with an L2 cache policy.
+__device__ __forceinline__ void st_global_hint(float* p, float2 v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(p), "f"(v.x), "f"(v.y), "l"(policy)
+               : "memory");
+}
+__device__ __forceinline__ void st_global_hint(float* p, float4 v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w), "l"(policy)
+               : "memory");
+}
+
 // As bulk_copy_g2s, with an L2 cache policy for the source lines.
 __device__ __forceinline__ void bulk_copy_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                                    uint64_t policy) {
