@@ -108,6 +108,7 @@ def test_paged_attention_matches_oracle(H, D, bs, dtype):
     (130, lambda r, B: r.integers(1, 449, B)),              # more sequences than SMs
     (700, lambda r, B: r.integers(0, 40, B)),               # many short / empty sequences
     (4, lambda r, B: np.array([4096, 1500, 37, 1030])),     # more than 32 items per sequence
+    (3, lambda r, B: np.array([512, 513, 480])),            # 16 items (merged in registers), 17 (two passes)
 ])
 def test_paged_attention_partitions(B, ctx_fn):
     rng = np.random.default_rng(B)
