@@ -12,7 +12,9 @@
 // of a persistent grid streams an equal share through an S-stage mbarrier ring.  Each
 // warp keeps its own online-softmax state over the rows it reads; at the end of a pair
 // the warps are merged in shared memory, and pairs split across CTAs are merged by the
-// last CTA to arrive (arrival counter, no spinning).
+// last CTA to arrive (arrival counter, no spinning).  The K/V stream is read under an L2
+// evict-first policy and the split partials are stored evict-last, so the partials are
+// still in L2 when the last CTA reads them back.
 #include "spd_params.cuh"
 
 namespace spd {
@@ -125,6 +127,7 @@ __global__ void __launch_bounds__(288) cross_attn_kernel(const CrossParams p) {
   // ---- producer warp ---------------------------------------------------------------
   if (warp == NW) {
     if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
       int pb = upper_index_i32(prefix, B, start);
       int s = 0;
       uint32_t ph = 0;
@@ -146,8 +149,8 @@ __global__ void __launch_bounds__(288) cross_attn_kernel(const CrossParams p) {
         const uint32_t qbytes = seg_first ? (uint32_t)(D * sizeof(T)) : 0u;
         T* dst = ring + (size_t)s * stage_elems;
         mbar_arrive_expect_tx(&full[s], 2 * bytes + qbytes);
-        bulk_copy_g2s(dst, kg + src, bytes, &full[s]);
-        bulk_copy_g2s(dst + unit_elems, vg + src, bytes, &full[s]);
+        bulk_copy_g2s_hint(dst, kg + src, bytes, &full[s], pol);
+        bulk_copy_g2s_hint(dst + unit_elems, vg + src, bytes, &full[s], pol);
         if (seg_first) bulk_copy_g2s(dst + 2 * unit_elems, qg + ((size_t)pb * H + h) * D, qbytes, &full[s]);
         issued = u + 1;
         if (++s == S) {
@@ -298,14 +301,17 @@ __global__ void __launch_bounds__(288) cross_attn_kernel(const CrossParams p) {
         const int nparts = c_last - c_first + 1;
         float* slot = p.partials + (size_t)(pair + c) * (D + 2);
         if (warp == 0) {
+          const uint64_t keep = l2_policy_evict_last();
           if (rg == 0) {
+            if constexpr (DPV % 2 == 0) {
 #pragma unroll
-            for (int i = 0; i < DPV; ++i) slot[dl * DPV + i] = o[i];
+              for (int i = 0; i < DPV; i += 2) st_global_hint(slot + dl * DPV + i, make_float2(o[i], o[i + 1]), keep);
+            } else {
+#pragma unroll
+              for (int i = 0; i < DPV; ++i) slot[dl * DPV + i] = o[i];
+            }
           }
-          if (lane == 0) {
-            slot[D] = M;
-            slot[D + 1] = L;
-          }
+          if (lane == 0) st_global_hint(slot + D, make_float2(M, L), keep);
         }
         named_sync(kCrossComputeBarrier, NCT);
         if (tid == 0) {
