@@ -24,6 +24,20 @@ __global__ void __launch_bounds__(256) add_layernorm_kernel(const AddLnParams p)
   const int nvec = p.cols / E;
   const T* x = reinterpret_cast<const T*>(p.x) + row * p.cols;
   const T* dl = p.delta ? reinterpret_cast<const T*>(p.delta) + row * p.cols : nullptr;
+  // gamma and beta do not depend on the row: with few vectors per lane they are loaded up
+  // front, so their latency overlaps the row's loads and reductions instead of following them
+  constexpr bool kPrefetch = VPL <= 4;
+  uint4 gpre[kPrefetch ? VPL : 1], bpre[kPrefetch ? VPL : 1];
+  if constexpr (kPrefetch) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) {
+        gpre[i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.gamma) + vi * E);
+        bpre[i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.beta) + vi * E);
+      }
+    }
+  }
   float v[VPL][E];
   float sum = 0.f;
 #pragma unroll
@@ -64,8 +78,14 @@ __global__ void __launch_bounds__(256) add_layernorm_kernel(const AddLnParams p)
   for (int i = 0; i < VPL; ++i) {
     const int vi = lane + 32 * i;
     if (vi >= nvec) continue;
-    const uint4 gv = *reinterpret_cast<const uint4*>(g + vi * E);
-    const uint4 bv = *reinterpret_cast<const uint4*>(bt + vi * E);
+    uint4 gv, bv;
+    if constexpr (kPrefetch) {
+      gv = gpre[i];
+      bv = bpre[i];
+    } else {
+      gv = *reinterpret_cast<const uint4*>(g + vi * E);
+      bv = *reinterpret_cast<const uint4*>(bt + vi * E);
+    }
     const T* ge = reinterpret_cast<const T*>(&gv);
     const T* be = reinterpret_cast<const T*>(&bv);
     alignas(16) T o[E];
