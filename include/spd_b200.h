@@ -36,6 +36,9 @@
  *   spd_add_layernorm      the residual add and the LayerNorm after it in every decoder
  *                          layer, speech_serving/models.py:163-207 (x = residual + ...;
  *                          norm2 / norm3), and transformers' WhisperDecoderLayer
+ *   spd_argmax_rows        the greedy pick after the output projection:
+ *                          speech_serving/graph_decode_buffers.py:446-448 (suppress mask,
+ *                          argmax) and speech_serving/models.py:487
  */
 #ifndef SPD_B200_H
 #define SPD_B200_H
@@ -165,6 +168,13 @@ int spd_cross_kv_project(const void* enc_out, const void* w_kv, const void* b_kv
  * mean and var (biased) in fp32 over the rounded x_out; x_out may alias x. */
 int spd_add_layernorm(const void* x, const void* delta, const void* gamma, const void* beta,
                       void* x_out, void* y, int rows, int cols, float eps, int dtype, void* stream);
+
+/* Greedy token pick: out[r] = the first c < cols maximising x[r*ld + c], where a column
+ * with skip_mask[c] != 0 (uint8 [cols], or NULL) scores -inf and a NaN beats any number;
+ * the same index as torch.argmax(x[:, :cols].masked_fill(skip_mask, -inf), dim=-1).
+ * out is int64 [rows]; ld >= cols (elements between rows). */
+int spd_argmax_rows(const void* x, int rows, int cols, int64_t ld, const void* skip_mask, int64_t* out,
+                    int dtype, void* stream);
 
 /* Allocation-free variant of spd_paged_decode_attn, for callers that cannot allocate
  * GPU memory or own a workspace: code running where cudaMalloc is unavailable or

@@ -129,6 +129,81 @@ static int add_ln_dispatch(const AddLnParams& p, cudaStream_t st) {
   return cudaPeekAtLastError() == cudaSuccess ? SPD_OK : SPD_ERR_CUDA;
 }
 
+// ------------------------------------------------------------------ greedy token pick
+// out[r] = argmax_c x[r][c] over c < cols, a column with skip[c] != 0 counting as -inf:
+// the same index as torch.argmax(x.masked_fill(skip, -inf), dim=-1), i.e. the first
+// maximal column, and the first NaN when a row holds one (the reference's greedy step,
+// speech_serving/models.py:598-610: suppress mask, then argmax over the vocabulary).
+// One CTA per row; each thread scans 16-byte vectors, then the CTA reduces (value, index).
+struct ArgBest {
+  float v;
+  int i;
+};
+
+// a beats b: NaN over numbers, larger value, then the lower index
+__device__ __forceinline__ bool arg_better(float av, int ai, float bv, int bi) {
+  const bool an = av != av, bn = bv != bv;
+  if (an || bn) return an && (!bn || ai < bi);
+  return av > bv || (av == bv && ai < bi);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const ArgmaxParams p) {
+  constexpr int E = 16 / sizeof(T);
+  const T* x = reinterpret_cast<const T*>(p.x) + (long long)blockIdx.x * p.ld;
+  const unsigned char* skip = reinterpret_cast<const unsigned char*>(p.skip);
+  ArgBest best{-INFINITY, 0x7fffffff};
+  auto consider = [&](float v, int c) {
+    if (skip && skip[c]) v = -INFINITY;
+    if (arg_better(v, c, best.v, best.i)) best = ArgBest{v, c};
+  };
+  if (p.vec) {
+    for (int c0 = threadIdx.x * E; c0 < p.cols; c0 += blockDim.x * E) {
+      if (c0 + E <= p.cols) {
+        const uint4 w = *reinterpret_cast<const uint4*>(x + c0);
+        const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+        for (int k = 0; k < E; ++k) consider(Elem<T>::to_f(e[k]), c0 + k);
+      } else {
+        for (int c = c0; c < p.cols; ++c) consider(Elem<T>::to_f(x[c]), c);
+      }
+    }
+  } else {
+    for (int c = threadIdx.x; c < p.cols; c += blockDim.x) consider(Elem<T>::to_f(x[c]), c);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, best.i, o);
+    if (arg_better(ov, oi, best.v, best.i)) best = ArgBest{ov, oi};
+  }
+  __shared__ ArgBest warp_best[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) warp_best[warp] = best;
+  __syncthreads();
+  if (warp == 0) {
+    best = lane < (int)(blockDim.x >> 5) ? warp_best[lane] : ArgBest{-INFINITY, 0x7fffffff};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, best.i, o);
+      if (arg_better(ov, oi, best.v, best.i)) best = ArgBest{ov, oi};
+    }
+    if (lane == 0) p.out[blockIdx.x] = best.i;
+  }
+}
+
+int argmax_rows_launch(const ArgmaxParams& p, int dtype, cudaStream_t st) {
+  const unsigned threads = p.cols >= 8192 ? 1024u : 256u;
+  switch (dtype) {
+    case SPD_F32: argmax_rows_kernel<float><<<p.rows, threads, 0, st>>>(p); break;
+    case SPD_F16: argmax_rows_kernel<__half><<<p.rows, threads, 0, st>>>(p); break;
+    case SPD_BF16: argmax_rows_kernel<__nv_bfloat16><<<p.rows, threads, 0, st>>>(p); break;
+    default: return SPD_ERR_UNSUPPORTED;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? SPD_OK : SPD_ERR_CUDA;
+}
+
 int add_layernorm_launch(const AddLnParams& p, int dtype, cudaStream_t st) {
   switch (dtype) {
     case SPD_F32: return add_ln_dispatch<float>(p, st);

@@ -17,6 +17,7 @@ int cross_attn_launch(const CrossParams& p, int dtype, int D, int sms, cudaStrea
 int kv_append_launch(const AppendParams& p, int sms, cudaStream_t st);
 int block_gather_launch(const GatherParams& p, int sms, cudaStream_t st);
 int add_layernorm_launch(const AddLnParams& p, int dtype, cudaStream_t st);
+int argmax_rows_launch(const ArgmaxParams& p, int dtype, cudaStream_t st);
 int cross_kv_project_launch(const void* enc_out, const void* w_kv, const void* b_kv, void* out,
                             const int32_t* slot_ids, int B, int T, int d_model, int L, int H, int D,
                             int T_out, int64_t out_slot_stride, int dtype, int* err, int sms, cudaStream_t st);
@@ -267,6 +268,20 @@ int spd_add_layernorm(const void* x, const void* delta, const void* gamma, const
   const int rc = spd::add_layernorm_launch(p, dtype, static_cast<cudaStream_t>(stream));
   if (rc == SPD_ERR_UNSUPPORTED) return fail(rc, "spd_add_layernorm: row length not supported");
   if (rc != SPD_OK) return fail(rc, "spd_add_layernorm: launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return ok();
+}
+
+int spd_argmax_rows(const void* x, int rows, int cols, int64_t ld, const void* skip_mask, int64_t* out, int dtype,
+                    void* stream) {
+  const int eb = elem_bytes(dtype);
+  if (!eb) return fail(SPD_ERR_UNSUPPORTED, "spd_argmax_rows: dtype %d not supported", dtype);
+  if (!x || !out) return fail(SPD_ERR_INVALID_ARG, "spd_argmax_rows: null pointer");
+  if (rows < 0 || cols <= 0 || ld < cols) return fail(SPD_ERR_INVALID_ARG, "spd_argmax_rows: bad sizes");
+  if (rows == 0) return ok();
+  spd::ArgmaxParams p{x, skip_mask, reinterpret_cast<long long*>(out), rows, cols, (long long)ld,
+                      (aligned16(x) && (ld * eb) % 16 == 0) ? 1 : 0};
+  const int rc = spd::argmax_rows_launch(p, dtype, static_cast<cudaStream_t>(stream));
+  if (rc != SPD_OK) return fail(rc, "spd_argmax_rows: launch failed: %s", cudaGetErrorString(cudaGetLastError()));
   return ok();
 }
 

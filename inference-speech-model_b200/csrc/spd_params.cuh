@@ -63,6 +63,15 @@ struct AddLnParams {  // residual add + LayerNorm (decoder_layer_ops.cu)
   float eps;
 };
 
+struct ArgmaxParams {  // greedy token pick over rows (decoder_layer_ops.cu)
+  const void* x;
+  const void* skip;  // uint8 [cols] or null: columns scored as -inf
+  long long* out;    // int64 [rows]
+  int rows, cols;
+  long long ld;      // elements between rows
+  int vec;           // rows start 16-byte aligned: 16-byte loads
+};
+
 struct GatherParams {
   const unsigned char* pool;
   const int* block_tables;

@@ -275,8 +275,7 @@ class WhisperClassSpeechEncoderDecoderModel(nn.Module):
             x, h = ops.add_layernorm(x, layer.cross_attn_out(c.view(n, -1)), layer.norm3)
             nxt = layers[l + 1].norm1 if l + 1 < len(layers) else self.decoder_norm
             x, h = ops.add_layernorm(x, layer.mlp(h), nxt)
-        logits = F.linear(h, _padded_head(self, self.lm_head))[:, : self.vocab_size]
-        return torch.argmax(logits, dim=-1)
+        return ops.argmax_rows(F.linear(h, _padded_head(self, self.lm_head)), self.vocab_size)
 
 
 class PretrainedWhisperModel(nn.Module):
@@ -502,7 +501,6 @@ class PretrainedWhisperModel(nn.Module):
             x, h = ops.add_layernorm(x, ea.out_proj(c.view(n, -1)), layer.final_layer_norm)
             nxt = layers[l + 1].self_attn_layer_norm if l + 1 < len(layers) else dec.layer_norm
             x, h = ops.add_layernorm(x, layer.fc2(layer.activation_fn(layer.fc1(h))), nxt)
-        logits = F.linear(h, _padded_head(self, self.hf_model.proj_out))[:, : self.vocab_size]
-        if self.suppress_mask is not None:
-            logits = logits.masked_fill(self.suppress_mask, float("-inf"))
-        return torch.argmax(logits, dim=-1)
+        # the suppress mask and the argmax over the vocabulary in one kernel
+        return ops.argmax_rows(F.linear(h, _padded_head(self, self.hf_model.proj_out)), self.vocab_size,
+                               self.suppress_mask)

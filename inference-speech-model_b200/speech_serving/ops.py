@@ -347,3 +347,29 @@ def add_layernorm(x: torch.Tensor, delta: Optional[torch.Tensor], ln, out_y: Opt
                                     float(ln.eps), dtype_code(x.dtype), _stream_handle())
     N.check(rc, "spd_add_layernorm")
     return x, y
+
+
+def argmax_rows(x: torch.Tensor, cols: Optional[int] = None, skip: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Greedy pick over the first ``cols`` columns of each row of ``x`` [rows, ld]:
+    ``torch.argmax(x[:, :cols].masked_fill(skip, -inf), dim=-1)`` in one kernel (the first
+    maximal column; a NaN wins), with ``skip`` a bool [cols] mask or None.  Returns int64
+    [rows]."""
+    _require_cuda("argmax_rows", x, skip, out)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise RuntimeError("argmax_rows: x must be [rows, ld] with unit column stride")
+    rows = x.shape[0]
+    cols = x.shape[1] if cols is None else int(cols)
+    if not 0 < cols <= x.shape[1]:
+        raise RuntimeError(f"argmax_rows: cols {cols} outside [1, {x.shape[1]}]")
+    if skip is not None and (skip.dtype != torch.bool or skip.numel() < cols or not skip.is_contiguous()):
+        raise RuntimeError("argmax_rows: skip must be a contiguous bool mask of at least cols entries")
+    if out is None:
+        out = torch.empty(rows, dtype=torch.long, device=x.device)
+    elif out.dtype != torch.long or out.shape != (rows,) or not out.is_contiguous():
+        raise RuntimeError("argmax_rows: out must be a contiguous int64 [rows] tensor")
+    ld = x.stride(0) if rows > 1 else x.shape[1]
+    rc = N.load().spd_argmax_rows(x.data_ptr(), rows, cols, ld, _ptr(skip), out.data_ptr(), dtype_code(x.dtype),
+                                  _stream_handle())
+    N.check(rc, "spd_argmax_rows")
+    return out

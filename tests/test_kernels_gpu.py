@@ -375,3 +375,26 @@ def test_add_layernorm_matches_add_then_layernorm(dtype, cols):
     torch.testing.assert_close(y.float(), ref_y, atol=tol, rtol=0)
     _, y2 = ops.add_layernorm(ref_x.clone(), None, ln)
     torch.testing.assert_close(y2.float(), ref_y, atol=tol, rtol=0)
+
+
+# ----------------------------------------------------------------------------- greedy pick
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("cols,ld", [(51865, 51904), (51866, 51866), (1000, 1003), (7, 8)])
+def test_argmax_rows_matches_masked_torch_argmax(dtype, cols, ld):
+    """spd_argmax_rows == torch.argmax(x[:, :cols].masked_fill(mask, -inf), -1): ties to the
+    first column (values drawn from a few levels), masked columns, a NaN row, an all -inf
+    row, unaligned row strides."""
+    g = torch.Generator(device="cpu").manual_seed(cols + ld)
+    rows = 67
+    x = (torch.randint(0, 6, (rows, ld), generator=g).float() - 3.0).to(dtype).to(DEV)
+    x[5, 17 % cols] = float("nan")
+    x[5, 3 % cols] = float("nan")
+    x[9, :] = float("-inf")
+    mask = torch.zeros(cols, dtype=torch.bool)
+    mask[torch.randint(0, cols, (max(1, cols // 50),), generator=g)] = True
+    mask = mask.to(DEV)
+    for m in (None, mask):
+        ref = x[:, :cols] if m is None else x[:, :cols].masked_fill(m, float("-inf"))
+        want = torch.argmax(ref, dim=-1)
+        got = ops.argmax_rows(x, cols, m)
+        assert torch.equal(got, want), (got - want).nonzero()[:5]
