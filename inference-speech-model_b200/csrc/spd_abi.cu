@@ -101,11 +101,9 @@ size_t spd_paged_decode_attn_workspace_size(int B, int H, int D, int max_blocks,
 }
 
 size_t spd_cross_attn_workspace_size(int B, int H, int D, int device) {
-  const int sms = sm_count(device);
-  if (B <= 0 || H <= 0 || D <= 0 || sms <= 0) return 0;
-  const size_t grid = (size_t)sms * spd::kMaxCtasPerSm;
+  if (B <= 0 || H <= 0 || D <= 0 || sm_count(device) <= 0) return 0;
   return spd::kWsHeaderBytes + spd::round_up((size_t)B * H * 4, 256) +
-         spd::round_up(((size_t)B * H + grid) * (D + 2) * 4, 256);
+         spd::round_up((size_t)B * H * spd::kCrossMaxItems * (D + 2) * 4, 256);  // a partial row per item
 }
 
 int spd_read_error_word(const void* error_word, int32_t* host_word, void* stream) {
@@ -187,7 +185,7 @@ int spd_cross_attn(const void* q, const void* k, const void* v, const int32_t* v
   p.scale_log2 = scale * 1.4426950408889634f;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   p.err = reinterpret_cast<int*>(ws);
-  p.counters = reinterpret_cast<int*>(ws + spd::kWsHeaderBytes);
+  p.work = reinterpret_cast<int*>(ws + spd::kWsWorkOffset);
   p.partials = reinterpret_cast<float*>(ws + spd::kWsHeaderBytes + spd::round_up((size_t)B * H * 4, 256));
   const int rc = spd::cross_attn_launch(p, dtype, D, sms, static_cast<cudaStream_t>(stream));
   if (rc != SPD_OK) return fail(rc, "spd_cross_attn: launch failed: %s", cudaGetErrorString(cudaGetLastError()));

@@ -19,14 +19,16 @@ namespace spd {
 // Workspace layout (bytes): [0,256) header (int32 error word at 0), then counters,
 // then fp32 partial slots.  Sizes are rounded to 256 bytes.
 constexpr size_t kWsHeaderBytes = 256;
-// Upper bound on resident CTAs per SM that any attention launch uses; the partial-slot
-// region is sized for grid <= num_SMs * kMaxCtasPerSm.
+// Upper bound on resident CTAs per SM that any attention launch uses.
 constexpr int kMaxCtasPerSm = 4;
 // Paged attention work item: up to this many consecutive pool blocks of one sequence.
 constexpr int kItemUnits = 2;
+// Cross-attention work items per (b, h) pair at most (sizes its partial slots).
+constexpr int kCrossMaxItems = 6;
 // Block tables up to this size are bulk-copied into each CTA's shared memory.
 constexpr size_t kTableSmemMax = 16384;
-// Workspace header: error word at byte 0, the paged kernel's item counters at byte 128.
+// Workspace header: error word at byte 0, the attention kernels' work-queue counters at
+// byte 128.
 constexpr size_t kWsWorkOffset = 128;
 // Bounded wait: 2 s of %globaltimer.
 constexpr unsigned long long SPD_WAIT_NS = 2000000000ull;
@@ -138,8 +140,6 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
-// 1-D bulk async copy global -> shared (no multicast).  dst, src 16-byte aligned,
-// bytes a multiple of 16.  Completion is signalled as transaction bytes on `bar`.
 // L2 policy for data read once per launch (the K/V stream): its lines are the first to
 // be evicted, so the small inputs, partials and code that the next launch reads again
 // stay resident in L2.
@@ -177,6 +177,8 @@ __device__ __forceinline__ void bulk_copy_g2s_hint(void* dst, const void* src, u
       : "memory");
 }
 
+// 1-D bulk async copy global -> shared (no multicast).  dst, src 16-byte aligned,
+// bytes a multiple of 16.  Completion is signalled as transaction bytes on `bar`.
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
                                               uint64_t* bar) {
   asm volatile(

@@ -35,9 +35,10 @@ struct CrossParams {
   long long kv_batch_stride, kv_head_stride;  // elements
   float scale_log2;
   int* err;
-  int* counters;    // [B*H]
-  float* partials;  // [(B*H + grid) * (D + 2)]
+  int* work;        // [0] next item to take, [1] CTAs done taking (both left at zero)
+  float* partials;  // [B*H*kCrossMaxItems * (D + 2)]: one row per item
   int stages;
+  int item_units;   // units (of the kernel's row chunk) per work item
 };
 
 struct AppendParams {

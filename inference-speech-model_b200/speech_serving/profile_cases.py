@@ -2,6 +2,7 @@
 
     python -m speech_serving.profile_cases paged_cfg2 --launches 3
     python -m speech_serving.profile_cases cross_cfg3 --launches 3
+    python -m speech_serving.profile_cases cross_dec --launches 3
     python -m speech_serving.profile_cases proj_small --launches 3
     python -m speech_serving.profile_cases cross_cfg3 --time 50   # CUDA-event timing
 
@@ -53,6 +54,22 @@ def _cross(dev, sets):
     return lambda i: ops.cross_attention(*out[i % sets], scale=0.125, workspace=ws)
 
 
+def _cross_decode(dev, sets):
+    """Cross-attention as one layer of a batch-64 Whisper-small decode step reads it: fp16,
+    H=12, the graph-slot layout [slot, layer, k|v, H, 1500, D] (two layers), valid encoder
+    lengths U[100, 1500] (2-30 s of audio)."""
+    g = torch.Generator().manual_seed(0)
+    B, L, H, T, D = 64, 2, 12, 1500, 64
+    slots = torch.randn(B, L, 2, H, T, D, device=dev).half()
+    out = []
+    for i in range(sets):
+        valid = torch.randint(100, 1501, (B,), generator=g, dtype=torch.int32)
+        out.append((torch.randn(B, H, D, device=dev).half(), slots[:, i % L, 0], slots[:, i % L, 1], valid.to(dev)))
+    ws = ops.cross_attn_workspace(B, H, D, dev)
+    WORK["cross_dec"] = (sum(int(o[3].sum()) * H * D * 4 + 2 * B * H * D * 2 for o in out) / sets, "GB/s")
+    return lambda i: ops.cross_attention(*out[i % sets], scale=0.125, workspace=ws)
+
+
 def _proj(dev, sets, d, L, H):
     D, T = 64, 1500
     enc = [torch.randn(1, T, d, device=dev).bfloat16() for _ in range(sets)]
@@ -67,6 +84,7 @@ CASES = {
     "paged_cfg2": lambda dev, n: _paged(dev, n),
     "paged_big": lambda dev, n: _paged(dev, n, B=512, NB=16384, lo=448, name="paged_big"),
     "cross_cfg3": lambda dev, n: _cross(dev, n),
+    "cross_dec": lambda dev, n: _cross_decode(dev, n),
     "proj_small": lambda dev, n: _proj(dev, n, 768, 12, 12),
     "proj_large": lambda dev, n: _proj(dev, n, 1280, 32, 20),
 }
