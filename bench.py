@@ -197,7 +197,7 @@ def run_reference(args):
 SERVING = {
     "config1": dict(arch="whisper-class-tiny", dtype="float32", n=4, rate=None, out=(64, 64), mels=80,
                     desc="WhisperClassSpeechEncoderDecoderModel(4,4,6,384,80,51865) seed 0, fp32, 4 requests, "
-                         "64 tokens each, graph decode, direct handoff"),
+                         "64 tokens each, graph decode, direct handoff; median of 3 timed runs"),
     "config4": dict(arch="whisper-small", dtype="float16", n=256, rate=None, out=(20, 200), mels=80,
                     desc="random-init Whisper-small, fp16, 256-request burst, audio U[2,30] s, outputs U{20..200}"),
     "config5": dict(arch="whisper-large-v3", dtype="bfloat16", n=2048, rate=64.0, out=(20, 224), mels=128,
@@ -263,7 +263,12 @@ def serving_leg(name, n_req, dev, rank, world):
     sched.reset_telemetry()
     if world > 1:
         dist.barrier()
-    r = run_engine(sched, reqs, WHISPER_DEFAULT_PREFIX_TOKENS)
+    # config 1 is a 40 ms run, at the mercy of a single host hiccup: the median of three
+    runs = []
+    for _ in range(3 if name == "config1" else 1):
+        sched.reset_telemetry()
+        runs.append(run_engine(sched, reqs, WHISPER_DEFAULT_PREFIX_TOKENS))
+    r = sorted(runs, key=lambda x: x["wall_s"])[len(runs) // 2]
     wall_max = replicas.max_over_ranks(r["wall_s"])
     toks_all = replicas.sum_over_ranks(r["generated_tokens"])
     leaks = sched.dual_cache.decoder_bm.allocated_block_count
