@@ -263,6 +263,41 @@ def test_cross_attention_graph_slot_layout():
         assert _err(out, ref) <= ATOL_16
 
 
+@pytest.mark.parametrize("B,H,T,valid_fn", [
+    (3, 4, 6000, lambda r, B: np.array([6000, 5999, 2177])),    # long contexts: 6 items of 8 units
+    (300, 2, 1500, lambda r, B: r.integers(0, 200, B)),         # many one-item pairs, some empty
+    (2, 3, 1500, lambda r, B: np.array([0, 0])),                # nothing to attend to
+])
+def test_cross_attention_item_queue_edges(B, H, T, valid_fn):
+    """The dynamic item queue and the split-pair merge: item counts at the per-pair cap,
+    many tiny pairs, empty batches; three calls in a row on one workspace (the queue
+    counter is re-armed by each launch), the last one replayed from a CUDA graph."""
+    rng = np.random.default_rng(B * 7 + T)
+    D = 64
+    valid = valid_fn(rng, B).astype(np.int32)
+    q = _t((rng.standard_normal((B, H, D)) * 0.5).astype(np.float16))
+    k = _t((rng.standard_normal((B, H, T, D)) * 0.5).astype(np.float16))
+    v = _t((rng.standard_normal((B, H, T, D)) * 0.5).astype(np.float16))
+    ref = O.cross_attention(_np32(q), _np32(k), _np32(v), valid)
+    ws = ops.cross_attn_workspace(B, H, D, q.device)
+    tv = _t(valid)
+    out = torch.full_like(q, float("nan"))
+    for _ in range(2):
+        ops.cross_attention(q, k, v, tv, out=out, workspace=ws)
+        assert _err(out, ref) <= ATOL_16
+    out.fill_(float("nan"))
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        ops.cross_attention(q, k, v, tv, out=out, workspace=ws)
+    g.replay()
+    g.replay()
+    torch.cuda.synchronize()
+    assert _err(out, ref) <= ATOL_16
+    assert ops.read_error_word(ws) == 0
+
+
 def test_cross_attention_config3_full_size():
     """B=128, H=20, D=64, 1500 positions, valid ~ U[300,1500], bf16."""
     g = torch.Generator().manual_seed(3)
