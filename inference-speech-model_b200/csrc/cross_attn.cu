@@ -54,7 +54,7 @@ struct CrossStage {
   int b;      // sequence, or -1: no more work
   int h;      // head
   int j;      // unit within the pair
-  int item;   // global item index
+  int item;   // item of the pair (0, 1, ...)
   int flags;  // kCrossFirst | kCrossLast
   int pad0, pad1, pad2;
 };
@@ -80,8 +80,9 @@ __global__ void __launch_bounds__(288) cross_attn_kernel(const CrossParams p) {
   uint64_t* empty = full + S;
   CrossStage* meta = reinterpret_cast<CrossStage*>(empty + S);  // [S]
   float* merge = reinterpret_cast<float*>(meta + S);             // [NW][D + 2]
-  int* ip = reinterpret_cast<int*>(merge + NW * (D + 2));        // [B + 1] item prefix (H items per step)
-  int* nch_s = ip + B + 1;                                       // [B] units per pair
+  int* ip = reinterpret_cast<int*>(merge + NW * (D + 2));        // [B + 1] item prefix over sequences
+  int* qp = ip + B + 1;                                          // [B + 1] queued-item prefix
+  int* nch_s = qp + B + 1;                                       // [B] units per pair
   int* val_s = nch_s + B;                                        // [B] clamped valid length
   int* flag = val_s + B;                                         // [0] abort
 
@@ -102,91 +103,130 @@ __global__ void __launch_bounds__(288) cross_attn_kernel(const CrossParams p) {
     fence_barrier_init();
     flag[0] = 0;
   }
-  // ---- 1. items per pair and their prefix over sequences ------------------------------
+  __syncthreads();
+
+  // producer state (lane 0 of warp NW)
+  const int G = (int)gridDim.x, P = B * H;
+  int s_p = 0;
+  uint32_t ph_p = 0;
+  long long n_issued = 0;
+  bool alive = true;
+  const uint64_t pol = l2_policy_evict_first();
+  // stages the units of item k of pair (b, h): units [k*N, min((k+1)*N, nch)) of valid length v
+  auto issue_item = [&](int b, int h, int k, int v, int nch) {
+    const int j0 = k * N, j1 = min(j0 + N, nch);
+    for (int j = j0; j < j1; ++j) {
+      if (n_issued >= S && (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&empty[s_p], ph_p ^ 1, p.err))) {
+        flag[0] = 1;
+        alive = false;
+        return;
+      }
+      const int nrows = min(C, v - j * C);
+      const size_t src = (size_t)b * p.kv_batch_stride + (size_t)h * p.kv_head_stride + (size_t)j * C * D;
+      const uint32_t bytes = (uint32_t)(nrows * D * (int)sizeof(T));
+      const bool first = (j == j0);
+      const uint32_t qbytes = first ? (uint32_t)(D * sizeof(T)) : 0u;
+      meta[s_p] = CrossStage{b, h, j, k, (first ? kCrossFirst : 0) | (j == j1 - 1 ? kCrossLast : 0), 0, 0, 0};
+      T* dst = ring + (size_t)s_p * stage_elems;
+      mbar_arrive_expect_tx(&full[s_p], 2 * bytes + qbytes);
+      bulk_copy_g2s_hint(dst, kg + src, bytes, &full[s_p], pol);
+      bulk_copy_g2s_hint(dst + unit_elems, vg + src, bytes, &full[s_p], pol);
+      if (first) bulk_copy_g2s(dst + 2 * unit_elems, qg + ((size_t)b * H + h) * D, qbytes, &full[s_p]);
+      ++n_issued;
+      if (++s_p == S) {
+        s_p = 0;
+        ph_p ^= 1;
+      }
+    }
+  };
+  // CTA g starts on item 0 of pair g, located with one direct load: its copies go out while
+  // the lengths are scanned.  Before the compute warps run nothing frees a stage, so an
+  // item with more units than the ring has stages waits until after the scan.
+  int v0 = 0, nch0 = 0;
+  if (warp == NW && lane == 0 && (int)blockIdx.x < P) {
+    v0 = clamp_valid(p.valid_lens[(int)blockIdx.x / H], p.T_max);
+    nch0 = (v0 + C - 1) / C;
+    if (v0 > 0 && min(N, nch0) <= S) {
+      issue_item((int)blockIdx.x / H, (int)blockIdx.x % H, 0, v0, nch0);
+      v0 = 0;  // issued
+    }
+  }
+
+  // ---- 1. items per pair: their prefix over sequences, and that of the queued ones (all
+  //      but the items CTAs started on) ----------------------------------------------------
   for (int i = tid; i < B; i += blockDim.x) {
     const int raw = p.valid_lens[i];
     if (raw > p.T_max) set_error(p.err, SPD_DEVERR_LENGTH);
     const int v = clamp_valid(raw, p.T_max);
     val_s[i] = v;
     nch_s[i] = (v + C - 1) / C;
-    ip[i + 1] = (nch_s[i] + N - 1) / N * H;
+    const int ib = (nch_s[i] + N - 1) / N;
+    const int started = v > 0 ? min(max(G - i * H, 0), H) : 0;
+    ip[i + 1] = ib * H;
+    qp[i + 1] = ib * H - started;
   }
-  if (tid == 0) ip[0] = 0;
+  if (tid == 0) {
+    ip[0] = 0;
+    qp[0] = 0;
+  }
   __syncthreads();
-  if (warp == 0) {
+  if (warp < 2) {
+    int* pre = warp == 0 ? ip : qp;
     int carry = 0;
     for (int base = 0; base < B; base += 32) {
       const int i = base + lane;
-      int v = (i < B) ? ip[i + 1] : 0;
+      int v = (i < B) ? pre[i + 1] : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int n = __shfl_up_sync(0xffffffffu, v, o);
         if (lane >= o) v += n;
       }
-      if (i < B) ip[i + 1] = v + carry;
+      if (i < B) pre[i + 1] = v + carry;
       carry += __shfl_sync(0xffffffffu, v, 31);
     }
   }
   __syncthreads();
-  const int n_items = ip[B];
   for (int b = blockIdx.x; b < B; b += gridDim.x) {
     if (val_s[b] == 0) {
       for (int i = tid; i < H * D; i += blockDim.x) out[(size_t)b * H * D + i] = Elem<T>::from_f(0.f);
     }
   }
 
-  // ---- 2. producer warp ---------------------------------------------------------------
+  // ---- 2. producer warp: the queued items ------------------------------------------------
   if (warp == NW) {
     if (lane == 0) {
-      const uint64_t pol = l2_policy_evict_first();
-      int s = 0;
-      uint32_t ph = 0;
-      long long n_issued = 0;
-      bool alive = true;
-      int item = blockIdx.x;
-      while (alive && item < n_items) {
-        const int nxt = (int)gridDim.x + atomicAdd(next_item, 1);  // next take, in flight meanwhile
-        const int b = upper_index_i32(ip, B, item);
+      if (v0 > 0) issue_item((int)blockIdx.x / H, (int)blockIdx.x % H, 0, v0, nch0);  // deferred first item
+      const int n_queue = qp[B];
+      int q = atomicAdd(next_item, 1);
+      while (alive && q < n_queue) {
+        const int nxt = atomicAdd(next_item, 1);  // next take, in flight meanwhile
+        const int b = upper_index_i32(qp, B, q);
         const int ib = (nch_s[b] + N - 1) / N;  // items of each pair of sequence b
-        const int r = item - ip[b];
-        const int h = r / ib, k = r % ib;
-        const int j0 = k * N, j1 = min(j0 + N, nch_s[b]);
-        for (int j = j0; j < j1; ++j) {
-          if (n_issued >= S && (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&empty[s], ph ^ 1, p.err))) {
-            flag[0] = 1;
-            alive = false;
-            break;
-          }
-          const int nrows = min(C, val_s[b] - j * C);
-          const size_t src = (size_t)b * p.kv_batch_stride + (size_t)h * p.kv_head_stride + (size_t)j * C * D;
-          const uint32_t bytes = (uint32_t)(nrows * D * (int)sizeof(T));
-          const bool first = (j == j0);
-          const uint32_t qbytes = first ? (uint32_t)(D * sizeof(T)) : 0u;
-          meta[s] = CrossStage{b, h, j, item, (first ? kCrossFirst : 0) | (j == j1 - 1 ? kCrossLast : 0), 0, 0, 0};
-          T* dst = ring + (size_t)s * stage_elems;
-          mbar_arrive_expect_tx(&full[s], 2 * bytes + qbytes);
-          bulk_copy_g2s_hint(dst, kg + src, bytes, &full[s], pol);
-          bulk_copy_g2s_hint(dst + unit_elems, vg + src, bytes, &full[s], pol);
-          if (first) bulk_copy_g2s(dst + 2 * unit_elems, qg + ((size_t)b * H + h) * D, qbytes, &full[s]);
-          ++n_issued;
-          if (++s == S) {
-            s = 0;
-            ph ^= 1;
-          }
+        const int hs = val_s[b] > 0 ? min(max(G - b * H, 0), H) : 0;  // pairs whose item 0 was started
+        const int r = q - qp[b];
+        int h, k;
+        if (ib > 1 && r < hs * (ib - 1)) {
+          h = r / (ib - 1);
+          k = 1 + r % (ib - 1);
+        } else {
+          const int r2 = r - hs * (ib - 1);
+          h = hs + r2 / ib;
+          k = r2 % ib;
         }
-        item = nxt;
+        issue_item(b, h, k, val_s[b], nch_s[b]);
+        q = nxt;
       }
       // end-of-work stage for the compute warps
-      if (alive && n_issued >= S && !mbar_wait_bounded(&empty[s], ph ^ 1, p.err)) alive = false;
+      if (alive && n_issued >= S && !mbar_wait_bounded(&empty[s_p], ph_p ^ 1, p.err)) alive = false;
       if (alive) {
-        meta[s] = CrossStage{-1, 0, 0, 0, 0, 0, 0, 0};
-        mbar_arrive(&full[s]);
+        meta[s_p] = CrossStage{-1, 0, 0, 0, 0, 0, 0, 0};
+        mbar_arrive(&full[s_p]);
       } else {
         flag[0] = 1;
       }
       // this CTA takes no more items; the last CTA to get here re-arms the counter
       __threadfence();
-      if (atomicAdd(done_ctas, 1) == (int)gridDim.x - 1) {
+      if (atomicAdd(done_ctas, 1) == G - 1) {
         *((volatile int*)next_item) = 0;
         *((volatile int*)done_ctas) = 0;
         __threadfence();
@@ -323,7 +363,8 @@ __global__ void __launch_bounds__(288) cross_attn_kernel(const CrossParams p) {
           for (int i = 0; i < DPV; ++i) op[i] = Elem<T>::from_f(o[i] * inv);
         }
       } else {  // a partial for the merge kernel, kept in L2
-        float* slot = p.partials + (size_t)mt.item * (D + 2);
+        const int ib = (nch_s[b] + N - 1) / N;
+        float* slot = p.partials + ((size_t)ip[b] + (size_t)h * ib + mt.item) * (D + 2);
         const uint64_t keep = l2_policy_evict_last();
         if (rg == 0) {
           if constexpr (DPV % 2 == 0) {
@@ -426,7 +467,7 @@ static int launch_cross(const CrossParams& base, int sms, cudaStream_t stream) {
   S = S < 2 ? 2 : (S > 8 ? 8 : S);
   p.stages = S;
   const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * (size_t)S + sizeof(CrossStage) * (size_t)S +
-                      4 * (size_t)Gm::NW * (D + 2) + 4 * (3 * (size_t)p.B + 5);
+                      4 * (size_t)Gm::NW * (D + 2) + 4 * (4 * (size_t)p.B + 6);
   if (smem > 227 * 1024) return SPD_ERR_UNSUPPORTED;
   auto kfn = cross_attn_kernel<T, D>;
   if (smem > 48 * 1024 &&
