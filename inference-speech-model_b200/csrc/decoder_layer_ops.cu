@@ -16,7 +16,7 @@ namespace spd {
 
 // VPL: 16-byte vectors per lane (a row of up to 32 * VPL vectors).
 template <typename T, int VPL>
-__global__ void __launch_bounds__(256) add_layernorm_kernel(const AddLnParams p) {
+__global__ void __launch_bounds__(128) add_layernorm_kernel(const AddLnParams p) {
   constexpr int E = 16 / sizeof(T);  // elements per vector
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
@@ -105,22 +105,23 @@ static int add_ln_dispatch(const AddLnParams& p, cudaStream_t st) {
   constexpr int E = 16 / sizeof(T);
   const int nvec = p.cols / E;
   const int vpl = (nvec + 31) / 32;
-  const unsigned grid = (unsigned)((p.rows + 7) / 8);
+  // four rows per CTA: a decode step's few rows spread over more SMs
+  const unsigned grid = (unsigned)((p.rows + 3) / 4);
   switch (vpl) {
-    case 1: add_layernorm_kernel<T, 1><<<grid, 256, 0, st>>>(p); break;
-    case 2: add_layernorm_kernel<T, 2><<<grid, 256, 0, st>>>(p); break;
-    case 3: add_layernorm_kernel<T, 3><<<grid, 256, 0, st>>>(p); break;
-    case 4: add_layernorm_kernel<T, 4><<<grid, 256, 0, st>>>(p); break;
-    case 5: case 6: add_layernorm_kernel<T, 6><<<grid, 256, 0, st>>>(p); break;
-    case 7: case 8: add_layernorm_kernel<T, 8><<<grid, 256, 0, st>>>(p); break;
+    case 1: add_layernorm_kernel<T, 1><<<grid, 128, 0, st>>>(p); break;
+    case 2: add_layernorm_kernel<T, 2><<<grid, 128, 0, st>>>(p); break;
+    case 3: add_layernorm_kernel<T, 3><<<grid, 128, 0, st>>>(p); break;
+    case 4: add_layernorm_kernel<T, 4><<<grid, 128, 0, st>>>(p); break;
+    case 5: case 6: add_layernorm_kernel<T, 6><<<grid, 128, 0, st>>>(p); break;
+    case 7: case 8: add_layernorm_kernel<T, 8><<<grid, 128, 0, st>>>(p); break;
     default:
       if constexpr (sizeof(T) == 4) {  // fp32 rows of up to 2048 elements
         if (vpl <= 12) {
-          add_layernorm_kernel<T, 12><<<grid, 256, 0, st>>>(p);
+          add_layernorm_kernel<T, 12><<<grid, 128, 0, st>>>(p);
           break;
         }
         if (vpl <= 16) {
-          add_layernorm_kernel<T, 16><<<grid, 256, 0, st>>>(p);
+          add_layernorm_kernel<T, 16><<<grid, 128, 0, st>>>(p);
           break;
         }
       }
