@@ -165,9 +165,12 @@ int spd_cross_kv_project(const void* enc_out, const void* w_kv, const void* b_kv
  * of 16 bytes, cols <= 2048):
  *   x_out[r] = round(x[r] + delta[r])                          (delta NULL: x_out unused)
  *   y[r]     = round((x_out[r] - mean) / sqrt(var + eps) * gamma + beta)
- * mean and var (biased) in fp32 over the rounded x_out; x_out may alias x. */
+ * mean and var (biased) in fp32 over the rounded x_out; x_out may alias x.  Row r of y
+ * starts at y + r * y_ld (0: y_ld = cols; y_ld * element size a multiple of 16 bytes),
+ * so y can be the leading columns of a wider buffer. */
 int spd_add_layernorm(const void* x, const void* delta, const void* gamma, const void* beta,
-                      void* x_out, void* y, int rows, int cols, float eps, int dtype, void* stream);
+                      void* x_out, void* y, int rows, int cols, int64_t y_ld, float eps, int dtype,
+                      void* stream);
 
 /* Greedy token pick: out[r] = the first c < cols maximising x[r*ld + c], where a column
  * with skip_mask[c] != 0 (uint8 [cols], or NULL) scores -inf and a NaN beats any number;

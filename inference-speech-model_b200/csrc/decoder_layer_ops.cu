@@ -73,7 +73,7 @@ __global__ void __launch_bounds__(128) add_layernorm_kernel(const AddLnParams p)
   const T* g = reinterpret_cast<const T*>(p.gamma);
   const T* bt = reinterpret_cast<const T*>(p.beta);
   T* xo = reinterpret_cast<T*>(p.x_out) + row * p.cols;
-  T* y = reinterpret_cast<T*>(p.y) + row * p.cols;
+  T* y = reinterpret_cast<T*>(p.y) + row * p.y_ld;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int vi = lane + 32 * i;

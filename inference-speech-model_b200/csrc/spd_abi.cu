@@ -252,7 +252,7 @@ int spd_block_gather(const void* pool, const int32_t* block_tables, const int32_
 }
 
 int spd_add_layernorm(const void* x, const void* delta, const void* gamma, const void* beta, void* x_out, void* y,
-                      int rows, int cols, float eps, int dtype, void* stream) {
+                      int rows, int cols, int64_t y_ld, float eps, int dtype, void* stream) {
   const int eb = elem_bytes(dtype);
   if (!eb) return fail(SPD_ERR_UNSUPPORTED, "spd_add_layernorm: dtype %d not supported", dtype);
   if (!x || !gamma || !beta || !y || (delta && !x_out)) return fail(SPD_ERR_INVALID_ARG, "spd_add_layernorm: null pointer");
@@ -261,8 +261,12 @@ int spd_add_layernorm(const void* x, const void* delta, const void* gamma, const
       (delta && (!aligned16(delta) || !aligned16(x_out))))
     return fail(SPD_ERR_INVALID_ARG, "spd_add_layernorm: rows and pointers must be 16-byte aligned");
   if (cols > 2048) return fail(SPD_ERR_UNSUPPORTED, "spd_add_layernorm: rows of at most 2048 elements");
+  if (y_ld == 0) y_ld = cols;
+  if (y_ld < cols || (y_ld * eb) % 16)
+    return fail(SPD_ERR_INVALID_ARG, "spd_add_layernorm: y_ld %lld must be >= cols and a multiple of 16 bytes",
+                (long long)y_ld);
   if (rows == 0) return ok();
-  spd::AddLnParams p{x, delta, gamma, beta, x_out, y, rows, cols, eps};
+  spd::AddLnParams p{x, delta, gamma, beta, x_out, y, rows, cols, (long long)y_ld, eps};
   const int rc = spd::add_layernorm_launch(p, dtype, static_cast<cudaStream_t>(stream));
   if (rc == SPD_ERR_UNSUPPORTED) return fail(rc, "spd_add_layernorm: row length not supported");
   if (rc != SPD_OK) return fail(rc, "spd_add_layernorm: launch failed: %s", cudaGetErrorString(cudaGetLastError()));

@@ -61,6 +61,7 @@ struct AddLnParams {  // residual add + LayerNorm (decoder_layer_ops.cu)
   void* x_out;
   void* y;
   int rows, cols;
+  long long y_ld;  // elements between rows of y
   float eps;
 };
 

@@ -44,7 +44,7 @@ _SIGNATURES = {
                            _vp, _vp]),
     "spd_block_gather": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _i, _i, _vp, _vp]),
     "spd_cross_kv_project": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _i, _vp, _vp]),
-    "spd_add_layernorm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _i, _vp]),
+    "spd_add_layernorm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i64, _f, _i, _vp]),
     "spd_argmax_rows": (_i, [_vp, _i, _i, _i64, _vp, _vp, _i, _vp]),
     "spd_paged_decode_attn_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i, _vp, _vp,
                                            _vp, _vp]),

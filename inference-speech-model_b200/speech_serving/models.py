@@ -53,6 +53,38 @@ def _fused_qkv(model: nn.Module, projs, q_scale: float = 1.0):
     return out
 
 
+def _fused_qkv_aug(model: nn.Module, projs, q_scale: float = 1.0):
+    """``_fused_qkv`` with the bias folded into the GEMM: per layer W [3, d_in + 8, H*D]
+    whose row d_in holds the biases (rows d_in+1.. are zero), for an input whose column
+    d_in is 1 (``_qkv_input``).  One batched GEMM then gives q, k and v with their biases,
+    with no copy of a broadcast bias into the output first."""
+    base = _fused_qkv(model, projs, q_scale)
+    key = tuple(w.data_ptr() for w, _ in base) + (q_scale,)
+    cache = model.__dict__.get("_qkv_aug_cache")
+    if cache is not None and cache[0] == key and cache[2] is base:
+        return cache[1]
+    with torch.no_grad():
+        out = []
+        for w, bias in base:
+            pad = torch.zeros((3, 7, w.shape[2]), dtype=w.dtype, device=w.device)
+            out.append(torch.cat([w, bias, pad], dim=1).contiguous())
+    model.__dict__["_qkv_aug_cache"] = (key, out, base)
+    return out
+
+
+def _qkv_input(model: nn.Module, n: int, d: int, like: torch.Tensor) -> torch.Tensor:
+    """The q/k/v GEMM's input rows [n, d + 8]: columns [0, d) take the LayerNorm output,
+    column d is 1 (it picks up the bias row of ``_fused_qkv_aug``'s weights), the rest 0.
+    One buffer per batch size, kept on the model."""
+    bufs = model.__dict__.setdefault("_qkv_in", {})
+    key = (n, d, like.dtype, like.device)
+    if key not in bufs:
+        t = torch.zeros((n, d + 8), dtype=like.dtype, device=like.device)
+        t[:, d] = 1
+        bufs[key] = t
+    return bufs[key]
+
+
 def _scaled_linears(model: nn.Module, linears, scale: float):
     """(weight * scale, bias * scale) per Linear, cached like ``_fused_qkv``."""
     key = tuple((p.weight.data_ptr(), p.weight._version) for p in linears) + (scale,)
@@ -474,17 +506,19 @@ class PretrainedWhisperModel(nn.Module):
         # q, k and v of a layer as one batched GEMM; WhisperAttention's query scaling is
         # folded into the q weights when it is a power of two (exact), else applied after
         fold = math.log2(dec.layers[0].self_attn.scaling).is_integer()
-        fused = _fused_qkv(self, [(lay.self_attn.q_proj, lay.self_attn.k_proj, lay.self_attn.v_proj)
-                                  for lay in dec.layers], q_scale=dec.layers[0].self_attn.scaling if fold else 1.0)
+        fused = _fused_qkv_aug(self, [(lay.self_attn.q_proj, lay.self_attn.k_proj, lay.self_attn.v_proj)
+                                      for lay in dec.layers], q_scale=dec.layers[0].self_attn.scaling if fold else 1.0)
         cross_q = _scaled_linears(self, [lay.encoder_attn.q_proj for lay in dec.layers],
                                   dec.layers[0].encoder_attn.scaling) if fold else None
         layers = dec.layers
-        # each residual add runs fused with the LayerNorm after it (x is updated in place)
-        x, h = ops.add_layernorm(x.contiguous(), None, layers[0].self_attn_layer_norm)
+        # each residual add runs fused with the LayerNorm after it (x is updated in place);
+        # the LayerNorm before a self-attention writes straight into the q/k/v GEMM's input
+        d = self.hidden_dim
+        qkv_in = _qkv_input(self, n, d, x)
+        x, _ = ops.add_layernorm(x.contiguous(), None, layers[0].self_attn_layer_norm, out_y=qkv_in[:, :d])
         for l, layer in enumerate(layers):
             sa = layer.self_attn
-            w, bias = fused[l]
-            qkv = torch.baddbmm(bias, h.unsqueeze(0).expand(3, n, h.shape[-1]), w)  # [3, n, H*D]
+            qkv = torch.bmm(qkv_in.unsqueeze(0).expand(3, n, d + 8), fused[l])  # [3, n, H*D], biases included
             q = qkv[0] if fold else qkv[0] * sa.scaling
             q, k, v = q.view(n, H, D), qkv[1].view(n, H, D), qkv[2].view(n, H, D)
             a = ops.paged_decode_attention(q, st.key_pool[l], st.value_pool[l], st.block_tables[:n], st.ctx_lens[:n],
@@ -499,8 +533,11 @@ class PretrainedWhisperModel(nn.Module):
             c = ops.cross_attention(cq, st.cross_kv[:n, l, 0], st.cross_kv[:n, l, 1], st.cross_lens[:n], scale=1.0,
                                     workspace=st.cross_ws[n])
             x, h = ops.add_layernorm(x, ea.out_proj(c.view(n, -1)), layer.final_layer_norm)
-            nxt = layers[l + 1].self_attn_layer_norm if l + 1 < len(layers) else dec.layer_norm
-            x, h = ops.add_layernorm(x, layer.fc2(layer.activation_fn(layer.fc1(h))), nxt)
+            mlp = layer.fc2(layer.activation_fn(layer.fc1(h)))
+            if l + 1 < len(layers):
+                x, _ = ops.add_layernorm(x, mlp, layers[l + 1].self_attn_layer_norm, out_y=qkv_in[:, :d])
+            else:
+                x, h = ops.add_layernorm(x, mlp, dec.layer_norm)
         # the suppress mask and the argmax over the vocabulary in one kernel
         return ops.argmax_rows(F.linear(h, _padded_head(self, self.hf_model.proj_out)), self.vocab_size,
                                self.suppress_mask)

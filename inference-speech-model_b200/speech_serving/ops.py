@@ -333,7 +333,8 @@ def cross_kv_project(
 def add_layernorm(x: torch.Tensor, delta: Optional[torch.Tensor], ln, out_y: Optional[torch.Tensor] = None):
     """``x += delta`` (in place, rounded to x's dtype) and ``LayerNorm(x)`` in one kernel;
     ``ln`` is an ``nn.LayerNorm`` over the last dimension.  Returns (x, y).  With
-    ``delta`` None only y = LayerNorm(x) is computed."""
+    ``delta`` None only y = LayerNorm(x) is computed.  ``out_y`` may be a [rows, cols] view
+    of a wider row-major buffer (unit column stride)."""
     _require_cuda("add_layernorm", x, delta)
     cols = x.shape[-1]
     if not x.is_contiguous() or (delta is not None and (delta.shape != x.shape or not delta.is_contiguous())):
@@ -341,9 +342,14 @@ def add_layernorm(x: torch.Tensor, delta: Optional[torch.Tensor], ln, out_y: Opt
     w, b = ln.weight, ln.bias
     if w is None or b is None or w.dtype != x.dtype or b.dtype != x.dtype or (delta is not None and delta.dtype != x.dtype):
         raise RuntimeError("add_layernorm: one dtype for x, delta and the LayerNorm's weight and bias")
+    rows = x.numel() // cols
     y = torch.empty_like(x) if out_y is None else out_y
+    if out_y is not None and (y.dtype != x.dtype or y.shape[-1] != cols or y.numel() != x.numel() or y.stride(-1) != 1
+                              or (y.dim() > 1 and rows > 1 and y.dim() != 2)):
+        raise RuntimeError("add_layernorm: out_y must be [rows, cols] of x's dtype with unit column stride")
+    y_ld = y.stride(0) if (y.dim() == 2 and rows > 1) else cols
     rc = N.load().spd_add_layernorm(x.data_ptr(), _ptr(delta), w.data_ptr(), b.data_ptr(),
-                                    x.data_ptr() if delta is not None else None, y.data_ptr(), x.numel() // cols, cols,
+                                    x.data_ptr() if delta is not None else None, y.data_ptr(), rows, cols, y_ld,
                                     float(ln.eps), dtype_code(x.dtype), _stream_handle())
     N.check(rc, "spd_add_layernorm")
     return x, y

@@ -410,6 +410,12 @@ def test_add_layernorm_matches_add_then_layernorm(dtype, cols):
     torch.testing.assert_close(y.float(), ref_y, atol=tol, rtol=0)
     _, y2 = ops.add_layernorm(ref_x.clone(), None, ln)
     torch.testing.assert_close(y2.float(), ref_y, atol=tol, rtol=0)
+    # y into the leading columns of a wider buffer (the q/k/v GEMM input): same values,
+    # the columns beyond untouched
+    wide = torch.full((rows, cols + 8), 7.0, device=DEV, dtype=dtype)
+    ops.add_layernorm(x.clone(), d, ln, out_y=wide[:, :cols])
+    assert torch.equal(wide[:, :cols], y)
+    assert bool((wide[:, cols:] == 7).all())
 
 
 # ----------------------------------------------------------------------------- greedy pick
