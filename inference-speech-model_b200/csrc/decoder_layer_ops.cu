@@ -159,14 +159,26 @@ __global__ void __launch_bounds__(1024) argmax_rows_kernel(const ArgmaxParams p)
     if (arg_better(v, c, best.v, best.i)) best = ArgBest{v, c};
   };
   if (p.vec) {
-    for (int c0 = threadIdx.x * E; c0 < p.cols; c0 += blockDim.x * E) {
-      if (c0 + E <= p.cols) {
-        const uint4 w = *reinterpret_cast<const uint4*>(x + c0);
-        const T* e = reinterpret_cast<const T*>(&w);
+    // four vectors per thread in flight per round (a row is read once, from L2 or DRAM)
+    constexpr int U = 4;
+    const int step = (int)blockDim.x * E;
+    for (int c0 = threadIdx.x * E; c0 < p.cols; c0 += U * step) {
+      uint4 w[U];
 #pragma unroll
-        for (int k = 0; k < E; ++k) consider(Elem<T>::to_f(e[k]), c0 + k);
-      } else {
-        for (int c = c0; c < p.cols; ++c) consider(Elem<T>::to_f(x[c]), c);
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * step;
+        if (c + E <= p.cols) w[u] = *reinterpret_cast<const uint4*>(x + c);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * step;
+        if (c + E <= p.cols) {
+          const T* e = reinterpret_cast<const T*>(&w[u]);
+#pragma unroll
+          for (int k = 0; k < E; ++k) consider(Elem<T>::to_f(e[k]), c + k);
+        } else {
+          for (int cc = c; cc < p.cols; ++cc) consider(Elem<T>::to_f(x[cc]), cc);
+        }
       }
     }
   } else {
