@@ -16,8 +16,8 @@
 
 namespace spd {
 
-// Workspace layout (bytes): [0,256) header (int32 error word at 0), then counters,
-// then fp32 partial slots.  Sizes are rounded to 256 bytes.
+// Workspace layout (bytes): [0,256) header (int32 error word at 0, work-queue counters at
+// 128), then a [B*H] int region, then fp32 partial slots.  Sizes are rounded to 256 bytes.
 constexpr size_t kWsHeaderBytes = 256;
 // Upper bound on resident CTAs per SM that any attention launch uses.
 constexpr int kMaxCtasPerSm = 4;

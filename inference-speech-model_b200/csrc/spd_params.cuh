@@ -19,7 +19,7 @@ struct PagedParams {
   float scale_log2;  // scale * log2(e)
   int* err;          // workspace error word
   int* work;         // [0] next item to take, [1] CTAs done taking (both left at zero)
-  int* counters;     // [B * H] arrival counters per (sequence, head) (left at zero)
+  int* counters;     // [B * H] ints kept in the workspace layout; the current kernels leave them unused
   float* partials;   // [B * ceil(max_blocks / kItemUnits) * H * (D + 8)]
   int stages;
   int table_in_smem;  // the whole block table is bulk-copied into shared memory
