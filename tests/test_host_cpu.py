@@ -252,3 +252,25 @@ def test_hf_attention_patch_swaps_and_restores_forwards():
         patch_decoder(dec, PagedDecodeState(pools[:1], pools[:1], tables, lens), cross=False)
     with pytest.raises(ValueError):
         patch_decoder(dec, PagedDecodeState(pools, pools, tables, lens), cross=True)
+
+
+def test_qkv_bias_row_matches_separate_projections():
+    """The decode step's q/k/v GEMM carries the biases as one more weight row against a
+    ones column of its input: the same values as the three Linear layers (fp32, CPU)."""
+    from speech_serving.models import _fused_qkv_aug, _qkv_input
+
+    torch.manual_seed(5)
+    d, hd, n = 64, 64, 5
+    q, k, v = torch.nn.Linear(d, hd), torch.nn.Linear(d, hd, bias=False), torch.nn.Linear(d, hd)
+    holder = torch.nn.Module()
+    w = _fused_qkv_aug(holder, [(q, k, v)], q_scale=0.125)[0]
+    assert w.shape == (3, d + 8, hd)
+    h = torch.randn(n, d)
+    buf = _qkv_input(holder, n, d, h)
+    assert buf.shape == (n, d + 8) and bool((buf[:, d] == 1).all()) and bool((buf[:, d + 1:] == 0).all())
+    buf[:, :d] = h
+    got = torch.bmm(buf.unsqueeze(0).expand(3, n, d + 8), w)
+    with torch.no_grad():
+        want = torch.stack([q(h) * 0.125, k(h), v(h)])
+    torch.testing.assert_close(got, want, atol=1e-5, rtol=1e-5)
+    assert _qkv_input(holder, n, d, h) is buf  # one buffer per batch size
