@@ -148,6 +148,16 @@ def cpu_baseline(seconds: float = 10.0, threads: int | None = None):
             "sample": f"{n} config-2 batches (B=64, fp16 pools) in {dt:.1f} s, oracle/oracle.c OpenMP"}
 
 
+def bench_config(world: int) -> dict:
+    """The `config` object of both arms' JSON lines (identical for the same N)."""
+    return {"workload": "config 2: paged decode self-attention B=64 H=12 D=64 bs=16 ctx~U[1,448] "
+                        "4096-block pool per input set",
+            "global_batch": CFG2["B"] * world, "seq_len": CFG2["max_ctx"], "parallelism": f"replicas x{world}",
+            "l2": f"each step reads the next of {N_SETS} input sets (rank r: seeds 1000+97r .. 1000+97r+{N_SETS - 1}; "
+                  "~46 MB of K/V per set, > 126 MB L2 per rotation)",
+            "timing": "K timed steps after W warm-up steps, each step one batch of the workload"}
+
+
 def dist_setup(args):
     import torch
     import torch.distributed as dist
@@ -164,33 +174,113 @@ def dist_setup(args):
 
 
 def run_reference(args):
+    """The reference arm: the reference's arithmetic for this path on the host cores.  The
+    reference is PyTorch with no native CPU library, so the timed code is its math ported to
+    C (oracle/oracle.c, OpenMP over all host threads), over the same rotation of input sets as
+    our arm.  Under torchrun only rank 0 runs and prints."""
     world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from oracle import c_oracle
 
     threads = os.cpu_count()
-    d = make_inputs(1000)
-    a = [d["q"].numpy(), d["k_pool"].numpy(), d["v_pool"].numpy(), d["tables"].numpy(), d["ctx"].numpy()]
-    nbytes = algorithmic_bytes(d["ctx"])
-    for _ in range(args.warmup):
-        c_oracle.paged_decode_attention(*a, CFG2["scale"], threads=threads)
+    sets = []
+    for i in range(N_SETS):
+        d = make_inputs(1000 + i)
+        sets.append(([d["q"].numpy(), d["k_pool"].numpy(), d["v_pool"].numpy(), d["tables"].numpy(),
+                      d["ctx"].numpy()], algorithmic_bytes(d["ctx"])))
+    for i in range(args.warmup):
+        c_oracle.paged_decode_attention(*sets[i % N_SETS][0], CFG2["scale"], threads=threads)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        c_oracle.paged_decode_attention(*a, CFG2["scale"], threads=threads)
+    for i in range(args.steps):
+        c_oracle.paged_decode_attention(*sets[i % N_SETS][0], CFG2["scale"], threads=threads)
     dt = time.perf_counter() - t0
-    v = nbytes * args.steps / dt / 1e9
+    nbytes = sum(sets[i % N_SETS][1] for i in range(args.steps))
+    v = nbytes / dt / 1e9
     line = {"metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16 in, f32 arithmetic", "data": "synthetic",
-            "impl": "reference",
-            "config": {"workload": "config 2: paged decode self-attention B=64 H=12 D=64 bs=16 ctx~U[1,448]",
-                       "global_batch": CFG2["B"], "seq_len": CFG2["max_ctx"], "parallelism": "host threads"},
+            "impl": "reference", "config": bench_config(world),
+            "timing": "host wall clock around the K steps (rank 0 only under torchrun)",
             "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": f"{args.steps} config-2 batches, oracle/oracle.c OpenMP (the reference is "
-                                       "PyTorch with no native CPU library; this is its arithmetic ported to C)"},
+                             "sample": f"{args.steps} config-2 batches rotating over {N_SETS} input sets, "
+                                       "oracle/oracle.c OpenMP (the reference is PyTorch with no native CPU "
+                                       "library; this is its arithmetic ported to C)"},
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
+
+
+def ref_triton_leg(sets, steps: int, dev):
+    """The reference's own Triton kernel (`paged_decode_attention_kernel`,
+    scripts/evaluate_paging_variants.py:56-133 of the reference), launched as the reference
+    launches it (:632-642: grid (B, H), q pre-scaled, sm_scale 1.0, explicit strides) on the
+    same rotating config-2 sets, K launches in one CUDA graph, CUDA events.  Its source is
+    read, unmodified, from the reference checkout installed under baseline/_ref; only the
+    kernel's own definition is compiled (the script's module imports audio and model
+    libraries the kernel does not use)."""
+    import ast
+
+    import torch
+
+    path = REPO / "baseline" / "_ref" / "scripts" / "evaluate_paging_variants.py"
+    if not path.exists():
+        return {"unavailable": "reference checkout not installed under baseline/_ref"}
+    try:
+        import triton
+        import triton.language as tl
+
+        tree = ast.parse(path.read_text())
+        fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "paged_decode_attention_kernel")
+        ns = {"triton": triton, "tl": tl}
+        # compiled with the file's own name and line numbers, so triton reads the
+        # unmodified source lines from the file
+        exec(compile(ast.Module(body=[fn], type_ignores=[]), str(path), "exec"), ns)
+        kern = ns["paged_decode_attention_kernel"]
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"could not load the reference kernel: {type(e).__name__}: {e}"[:300]}
+    c = CFG2
+    B, H, D, bs = c["B"], c["H"], c["D"], c["bs"]
+    qs = [(s["q"] * c["scale"]).view(B, H, 1, D) for s in sets]  # exact: the scale is a power of two
+    outs = [torch.zeros(B, H, 1, D, dtype=torch.float16, device=dev) for _ in sets]
+
+    def launch(i):
+        j = i % len(sets)
+        s, q, o = sets[j], qs[j], outs[j]
+        kc, vc, t = s["k_pool"], s["v_pool"], s["tables"]
+        kern[(B, H)](q, kc, vc, t, s["ctx"], o, 1.0,
+                     q.stride(0), q.stride(1), q.stride(2), q.stride(3),
+                     kc.stride(0), kc.stride(1), kc.stride(2), kc.stride(3),
+                     vc.stride(0), vc.stride(1), vc.stride(2), vc.stride(3),
+                     t.stride(0), t.stride(1),
+                     o.stride(0), o.stride(1), o.stride(2), o.stride(3),
+                     BLOCK_SIZE=bs, HEAD_DIM=D)
+
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for i in range(len(sets)):
+            launch(i)  # compiles the kernel
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(steps):
+            launch(i)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        graph.replay()  # keeps the GPU busy while the timed replay is submitted
+        s0.record(stream)
+        graph.replay()
+        s1.record(stream)
+    torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1)
+    nbytes = sum(algorithmic_bytes(sets[i % len(sets)]["ctx"].cpu()) for i in range(steps))
+    del graph
+    return {"value": round(nbytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s", "launch_us": round(ms * 1e3 / steps, 3),
+            "source": "baseline/_ref/scripts/evaluate_paging_variants.py (unmodified kernel definition)",
+            "triton": triton.__version__, "outputs": outs}
 
 
 # ---------------------------------------------------------------------------- serving legs
@@ -203,7 +293,11 @@ SERVING = {
     "config5": dict(arch="whisper-large-v3", dtype="bfloat16", n=2048, rate=64.0, out=(20, 224), mels=128,
                     desc="random-init Whisper-large-v3, bf16, Poisson 64 req/s per GPU, audio U[2,30] s, "
                          "outputs U{20..224}"),
+    "config5_burst": dict(arch="whisper-large-v3", dtype="bfloat16", n=512, rate=None, out=(20, 224), mels=128,
+                          desc="capacity of the config-5 engine: random-init Whisper-large-v3, bf16, all requests "
+                               "arriving at once, audio U[2,30] s, outputs U{20..224}"),
 }
+AGREEMENT_SAMPLE = 64  # requests of rank 0 re-decoded by the HF decoder after a serving leg
 
 
 def _serving_model(cfg, dev):
@@ -230,9 +324,11 @@ def _serving_scheduler(model, dtype, dev, max_batch=64, dec_blocks=4096):
                                      graph_readback_k=4, graph_direct_encoder_kv=True)
 
 
-def serving_leg(name, n_req, dev, rank, world):
+def serving_leg(name, n_req, dev, rank, world, models):
     """Decoder tokens/s of one serving configuration: every rank serves its own request
-    stream (replicas); whole-job tokens/s = tokens of all ranks / slowest rank's wall."""
+    stream (replicas); whole-job tokens/s = tokens of all ranks / slowest rank's wall.
+    After the timed run, rank 0 re-decodes a sample of its requests with the unpatched HF
+    decoder (the reference's path) and reports how many sequences are identical."""
     import torch
     import torch.distributed as dist
     from speech_serving import replicas
@@ -240,7 +336,12 @@ def serving_leg(name, n_req, dev, rank, world):
     from speech_serving.serving import run_engine, synthetic_requests
 
     cfg = SERVING[name]
-    model, dtype = _serving_model(cfg, dev)
+    key = (cfg["arch"], cfg["dtype"])
+    if key not in models:
+        models.clear()  # one model at a time on the device
+        torch.cuda.empty_cache()
+        models[key] = _serving_model(cfg, dev)
+    model, dtype = models[key]
     sched = _serving_scheduler(model, dtype, dev, max_batch=min(64, max(4, n_req)))
     if name == "config1":
         gen = torch.Generator().manual_seed(1)
@@ -279,8 +380,21 @@ def serving_leg(name, n_req, dev, rank, world):
                                        "latency_p50_s", "latency_p95_s")},
            "leaked_decoder_blocks": leaks, "timing": "wall clock around the serving loop, synchronized both ends"}
     if name == "config1":
-        out["tokens"] = [q.generated_tokens for q in sorted(sched.completed, key=lambda q: q.id)]
-    del sched, model
+        out["tokens"] = r["tokens_by_request"]
+    elif rank == 0:
+        from speech_serving.hf_reference import hf_greedy_tokens, sequence_agreement
+
+        k = min(AGREEMENT_SAMPLE, len(reqs))
+        mels = torch.stack([q.mel for q in reqs[:k]])
+        ref = hf_greedy_tokens(model, mels, WHISPER_DEFAULT_PREFIX_TOKENS, [q.max_new_tokens for q in reqs[:k]],
+                               batch=32)
+        a = sequence_agreement(r["tokens_by_request"][:k], ref)
+        out["hf_sequence_agreement"] = {"requests": a["requests"], "identical": a["identical"],
+                                        "identical_frac": round(a["identical_frac"], 4),
+                                        "first_divergence": a["first_divergence"],
+                                        "sample": f"the first {k} requests of rank 0, re-decoded greedily by the "
+                                                  "unpatched HF decoder on the same weights, device and dtype"}
+    del sched
     torch.cuda.empty_cache()
     return out
 
@@ -315,6 +429,14 @@ def run_ours(args):
     world, rank, local = dist_setup(args)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if world > 1:
+        # every rank drives its own serving loop from the host: give each its own share of
+        # the host cores, so N schedulers and their intra-op thread pools do not compete
+        cores = sorted(os.sched_getaffinity(0))
+        per = max(1, len(cores) // world)
+        mine = cores[rank * per:(rank + 1) * per] or cores
+        os.sched_setaffinity(0, mine)
+        torch.set_num_threads(len(mine))
     from speech_serving import ops, replicas
 
     c = CFG2
@@ -360,6 +482,9 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
+            # one untimed replay first: the GPU works on it while the host submits the
+            # timed replay, so the host's graph-launch latency is not counted as GPU time
+            graph.replay()
             start.record(stream)
             graph.replay()
             end.record(stream)
@@ -369,6 +494,7 @@ def run_ours(args):
         sustain(0.6)
     ms = start.elapsed_time(end)
     ms_max = replicas.max_over_ranks(ms)
+    launch_us_ranks = [round(x * 1e3 / args.steps, 3) for x in replicas.gather_over_ranks(ms)]
     bytes_rank = sum(bytes_per[i % N_SETS] for i in range(args.steps))
     value = replicas.whole_job_rate(replicas.sum_over_ranks(bytes_rank), ms_max) / 1e9
     launch_ms = ms / args.steps
@@ -473,11 +599,26 @@ def run_ours(args):
             raise RuntimeError("kernel reported a device error during the benchmark")
 
     del graph
+    ref_triton = None
+    if rank == 0 and not args.no_ref_triton:
+        ref_triton = ref_triton_leg(sets, args.steps, dev)
+        if "outputs" in ref_triton:
+            # the reference kernel computes the same attention: its outputs agree with ours
+            tri = ref_triton.pop("outputs")
+            j = (args.steps - 1) % N_SETS
+            s_ = sets[j]
+            mine = ops.paged_decode_attention(s_["q"], s_["k_pool"], s_["v_pool"], s_["tables"], s_["ctx"],
+                                              scale=c["scale"], workspace=ws)
+            ref_triton["max_abs_diff_vs_ours"] = float((tri[j].view_as(mine).float() - mine.float()).abs().max())
+            ref_triton["frac"] = round(ref_triton["value"] / _peaks()[0], 4)
     serving = {}
     legs = [x for x in args.serving.split(",") if x and x != "none"]
+    models = {}
     for name in legs:
-        n_req = {"config1": 4, "config4": SERVING["config4"]["n"], "config5": args.config5_requests}[name]
-        serving[name] = serving_leg(name, n_req, dev, rank, world)
+        n_req = {"config1": 4, "config4": SERVING["config4"]["n"], "config5": args.config5_requests,
+                 "config5_burst": args.config5_burst_requests}[name]
+        serving[name] = serving_leg(name, n_req, dev, rank, world, models)
+    models.clear()
     if rank == 0 and world == 1 and "config1" in serving and not args.no_cpu_baseline:
         cb = serving_cpu_baseline()
         ours = serving["config1"].pop("tokens")
@@ -505,12 +646,10 @@ def run_ours(args):
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16 in, f32 arithmetic", "data": "synthetic",
-        "config": {"workload": "config 2: paged decode self-attention B=64 H=12 D=64 bs=16 ctx~U[1,448] "
-                               "4096-block pool per input set",
-                   "global_batch": CFG2["B"] * world, "seq_len": CFG2["max_ctx"], "parallelism": f"replicas x{world}",
-                   "l2": f"inputs rotate over {N_SETS} resident sets (~{N_SETS * bytes_per[0] / 1e6:.0f} MB touched "
-                         "per rotation > 126 MB L2)",
-                   "timing": "CUDA graph of K launches, CUDA events, max over ranks"},
+        "config": bench_config(world),
+        "timing": "the K steps replayed from one CUDA graph behind one untimed replay, CUDA events on the replay "
+                  "stream, barrier + synchronize on both sides, max over ranks",
+        "launch_us_per_rank": launch_us_ranks,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_source": f"{peak_kind} hbm_gbs (copy bandwidth)",
@@ -523,6 +662,7 @@ def run_ours(args):
         "gpu_launches": 2 * args.steps,  # streaming kernel + split merge kernel per step
         "clocks": sampler.summary(),
         "max_abs_err_vs_oracle": ok_err,
+        "ref_triton": ref_triton,
         "serving": serving,
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -538,10 +678,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--serving", default="config1,config4,config5",
-                    help="comma-separated serving legs (config1, config4, config5) or none")
-    ap.add_argument("--config5-requests", type=int, default=256,
-                    help="config-5 requests per rank (a bounded sample of the 2048-request stream)")
+    ap.add_argument("--no-ref-triton", action="store_true", help="skip timing the reference's Triton kernel")
+    ap.add_argument("--serving", default="config1,config4,config5,config5_burst",
+                    help="comma-separated serving legs (config1, config4, config5, config5_burst) or none")
+    ap.add_argument("--config5-requests", type=int, default=2048,
+                    help="config-5 requests per rank (the configuration's 2048-request Poisson stream, 32 s)")
+    ap.add_argument("--config5-burst-requests", type=int, default=512,
+                    help="requests per rank of the config-5 capacity leg (all arriving at once)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -187,11 +187,14 @@ int spd_argmax_rows(const void* x, int rows, int cols, int64_t ld, const void* s
  *   Same arguments and results as spd_paged_decode_attn, minus the workspace; the
  *   split-KV scratch lives in a 4 MiB array inside the library that every GPU using this
  *   entry point keeps until the process exits (SPD_NOALLOC_SCRATCH_BYTES).  Calls whose
- *   spd_paged_decode_attn_workspace_size(B, H, D, device) exceeds it are rejected with
- *   SPD_ERR_WORKSPACE (e.g. B=64, H=12, D=64, 28 blocks per table needs about 3.0 MiB).
- *   error_word: optional int32 device word that receives this call's SPD_DEVERR_* flags.
+ *   spd_paged_decode_attn_workspace_size(B, H, D, max_blocks, device) exceeds it are
+ *   rejected with SPD_ERR_WORKSPACE (e.g. B=64, H=12, D=64, 28 blocks per table needs
+ *   about 3.0 MiB); arguments are checked before the scratch is touched.
+ *   error_word: optional int32 device word; this call's SPD_DEVERR_* flags are OR-ed into
+ *   it (flags already there are kept).
  *   The first call on each device looks up the array's device address; make that first
- *   call before capturing any stream.  Every call clears the scratch counters it needs,
+ *   call before capturing any stream.  The address is cached for the process: calls after
+ *   a cudaDeviceReset are not supported.  Every call clears the scratch counters it needs,
  *   and all calls share one array: calls that overlap on the GPU (different streams, or
  *   several host threads) race and give wrong results. */
 #define SPD_NOALLOC_SCRATCH_BYTES (4u * 1024u * 1024u)

@@ -7,6 +7,12 @@ Every ``*.cu`` file in this directory is compiled to an object with
 into ``../lib/libspd_b200.so`` with the CUDA runtime linked statically, so the library
 carries no dependency on the CUDA runtime that the host process happens to load.
 Objects are rebuilt only when a source or header is newer than them.
+
+``python build.py --trace`` builds the trace variant instead: the same sources with
+SPD_TRACE_BUILD defined, objects under ``_build/trace``, linked into
+``../lib/libspd_b200_trace.so``.  Its kernels record a %globaltimer timeline of their
+last launch (csrc/spd_trace.cuh); profile_cases.py at the repository root loads it with
+``--trace``.  The normal library never contains these marks.
 """
 from __future__ import annotations
 
@@ -23,6 +29,8 @@ PKG = HERE.parent
 REPO = PKG.parent
 OBJ_DIR = PKG / "_build"
 LIB = PKG / "lib" / "libspd_b200.so"
+TRACE_OBJ_DIR = OBJ_DIR / "trace"
+TRACE_LIB = PKG / "lib" / "libspd_b200_trace.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
                      "--expt-relaxed-constexpr", "-I", str(REPO / "include"), "-I", str(HERE)]
@@ -42,17 +50,19 @@ def _stale(obj: Path, deps: list[Path]) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def build(verbose: bool = False, force: bool = False) -> Path:
-    OBJ_DIR.mkdir(parents=True, exist_ok=True)
-    LIB.parent.mkdir(parents=True, exist_ok=True)
+def build(verbose: bool = False, force: bool = False, trace: bool = False) -> Path:
+    obj_dir, lib = (TRACE_OBJ_DIR, TRACE_LIB) if trace else (OBJ_DIR, LIB)
+    flags = NVCC_FLAGS + (["-DSPD_TRACE_BUILD"] if trace else [])
+    obj_dir.mkdir(parents=True, exist_ok=True)
+    lib.parent.mkdir(parents=True, exist_ok=True)
     sources = sorted(HERE.glob("*.cu"))
     headers = sorted(HERE.glob("*.cuh")) + sorted((REPO / "include").glob("*.h"))
     cc = nvcc()
     jobs = []
     for src in sources:
-        obj = OBJ_DIR / (src.stem + ".o")
+        obj = obj_dir / (src.stem + ".o")
         if force or _stale(obj, [src] + headers):
-            cmd = [cc] + NVCC_FLAGS + (["-Xptxas", "-v"] if verbose else []) + ["-c", str(src), "-o", str(obj)]
+            cmd = [cc] + flags + (["-Xptxas", "-v"] if verbose else []) + ["-c", str(src), "-o", str(obj)]
             jobs.append((src, cmd))
     def run(job):
         src, cmd = job
@@ -67,19 +77,20 @@ def build(verbose: bool = False, force: bool = False) -> Path:
                 failed.append(src.name)
     if failed:
         raise RuntimeError(f"nvcc failed for: {', '.join(failed)}")
-    objs = [OBJ_DIR / (s.stem + ".o") for s in sources]
-    if force or jobs or not LIB.exists() or _stale(LIB, objs):
-        cmd = [cc] + ARCH + ["-shared", "-cudart", "static", "-o", str(LIB)] + [str(o) for o in objs]
+    objs = [obj_dir / (s.stem + ".o") for s in sources]
+    if force or jobs or not lib.exists() or _stale(lib, objs):
+        cmd = [cc] + ARCH + ["-shared", "-cudart", "static", "-o", str(lib)] + [str(o) for o in objs]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)
-            raise RuntimeError("linking libspd_b200.so failed")
-    return LIB
+            raise RuntimeError(f"linking {lib.name} failed")
+    return lib
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--force", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="build the %%globaltimer trace variant")
     a = ap.parse_args()
-    print(build(verbose=a.verbose, force=a.force))
+    print(build(verbose=a.verbose, force=a.force, trace=a.trace))

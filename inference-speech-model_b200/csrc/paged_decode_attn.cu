@@ -42,14 +42,18 @@
 // * Every wait is bounded; a warp whose wait runs out records SPD_DEVERR_TIMEOUT, raises
 //   the CTA's abort flag and leaves, and the others' bounded waits then run out too.
 #include <type_traits>
+#include <vector>
 
 #include "spd_params.cuh"
+#include "spd_trace.cuh"
 
-// Timeline hook: expands to nothing unless a tracing build defines it (to record
-// %globaltimer at marked points of each CTA).
-#ifndef SPD_TRACE
-#define SPD_TRACE(point) ((void)0)
-#endif
+// Timeline marks (trace builds only; see spd_trace.cuh).  Streaming kernel, per CTA:
+// 0 entry, 6 griddepcontrol.wait returned, 2 first copy issued, 1 lengths scanned,
+// 3 producer out of items, 4 first stage consumed (warp 0), 5 warp 0 done, 7 producer
+// done.  Merge kernel, per CTA: 0 entry, 1 griddepcontrol.wait returned, 2 done.
+SPD_TRACE_ARRAY
+#define SPD_TRACE(point) SPD_TRACE_AT(0, point)
+#define SPD_TRACE_MERGE(point) SPD_TRACE_AT(1, point)
 
 namespace spd {
 
@@ -127,7 +131,10 @@ struct StageMeta {
 };
 constexpr int kFirst = 1, kLast = 2, kAppend = 4;
 constexpr int kPairThreads = 416;  // two-CTA form: up to 12 compute warps + the producer
-constexpr int kPairMinSeqs = 128;  // batches at least this large use the two-CTA form
+#ifndef SPD_PAIR_MIN_SEQS
+#define SPD_PAIR_MIN_SEQS 128
+#endif
+constexpr int kPairMinSeqs = SPD_PAIR_MIN_SEQS;  // batches at least this large use the two-CTA form
 
 __device__ __forceinline__ int clamp_ctx(int c, int max_ctx) { return c > max_ctx ? max_ctx : (c > 0 ? c : 0); }
 
@@ -376,6 +383,7 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
           (void)mbar_wait_bounded(&full[u % S], (uint32_t)((u / S) & 1), nullptr);
         }
       }
+      SPD_TRACE(7);
     }
     return;
   }
@@ -585,8 +593,10 @@ __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
   const int MC = (p.max_blocks + kItemUnits - 1) / kItemUnits;
   const int ctx_b = live ? clamp_ctx(p.context_lens[b], max_ctx) : 0;
   const int nitems = ((ctx_b + BS - 1) / BS + kItemUnits - 1) / kItemUnits;
+  if (threadIdx.x == 0) SPD_TRACE_MERGE(0);
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the streaming kernel has finished
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (threadIdx.x == 0) SPD_TRACE_MERGE(1);
   if (!live || nitems <= 1) return;  // written by the streaming kernel (or zero)
   const float* base = p.partials + ((size_t)b * MC * p.H + h) * kPartialRow<D>;
   const size_t stride = (size_t)p.H * kPartialRow<D>;  // next item, same head
@@ -623,6 +633,7 @@ __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
         dst[3] = Elem<T>::from_f(o.w * inv);
       }
     }
+    if ((threadIdx.x & 31) == 0) SPD_TRACE_MERGE(2);
     return;
   }
   // long sequences: two passes over the items
@@ -754,3 +765,16 @@ int paged_decode_attn_launch(const PagedParams& p, int dtype, int D, int bs, int
 }
 
 }  // namespace spd
+
+#ifdef SPD_TRACE_BUILD
+// Trace builds only: copies the last launch's marks, [kernel][CTA][point] as unsigned
+// 64-bit %globaltimer values (0 where a mark was not reached), into `host` (synchronous).
+extern "C" int spd_trace_fetch_paged(unsigned long long* host, size_t count) {
+  const size_t n = (size_t)spd::kTraceKernels * spd::kTraceCtas * spd::kTracePoints;
+  if (!host || count < n) return SPD_ERR_INVALID_ARG;
+  if (cudaMemcpyFromSymbol(host, spd::g_trace, n * sizeof(unsigned long long)) != cudaSuccess) return SPD_ERR_CUDA;
+  std::vector<unsigned long long> zero(n, 0ull);
+  return cudaMemcpyToSymbol(spd::g_trace, zero.data(), n * sizeof(unsigned long long)) == cudaSuccess ? SPD_OK
+                                                                                                     : SPD_ERR_CUDA;
+}
+#endif

@@ -6,7 +6,8 @@
 // partial results.  This entry point keeps that scratch in a file-scope device array of
 // SPD_NOALLOC_SCRATCH_BYTES instead.  In host code `g_noalloc_scratch` only names the
 // symbol — it is not a device address — so each device's address is looked up once with
-// cudaGetSymbolAddress (with that device current) and cached.
+// cudaGetSymbolAddress (with that device current) and cached for the life of the process
+// (a cudaDeviceReset invalidates the cached address; calls after one are not supported).
 #include <cstdio>
 #include <mutex>
 
@@ -14,6 +15,9 @@
 
 namespace spd {
 int record_error(int code, const char* msg);
+int paged_decode_attn_check(const void* q, const void* k_pool, const void* v_pool, const int32_t* block_tables,
+                            const int32_t* context_lens, const void* out, int B, int H, int D, int block_size,
+                            int max_blocks, int num_blocks, int dtype, const void* k_new, const void* v_new);
 }
 
 namespace {
@@ -45,6 +49,13 @@ int scratch_for_current_device(void** out) {
   return SPD_OK;
 }
 
+// ORs this call's device error flags (the scratch header's word) into the caller's word,
+// which may carry flags from earlier calls or other ops.
+__global__ void or_error_word(int32_t* dst, const int32_t* src) {
+  const int32_t v = *src;
+  if (v) atomicOr(dst, v);
+}
+
 }  // namespace
 
 extern "C" int spd_paged_decode_attn_noalloc(const void* q, void* k_pool, void* v_pool,
@@ -52,9 +63,11 @@ extern "C" int spd_paged_decode_attn_noalloc(const void* q, void* k_pool, void* 
                                              void* out, int B, int H, int D, int block_size, int max_blocks,
                                              int num_blocks, float scale, int dtype, const void* k_new,
                                              const void* v_new, int32_t* error_word, void* stream) {
-  if (B <= 0 || H <= 0 || D <= 0 || max_blocks <= 0)
-    return spd::record_error(SPD_ERR_INVALID_ARG,
-                             "spd_paged_decode_attn_noalloc: B, H, D and max_blocks must be positive");
+  // every argument check comes before the shared scratch is touched: a refused call must
+  // not clear counters that a call still running on the GPU is using
+  int rc = spd::paged_decode_attn_check(q, k_pool, v_pool, block_tables, context_lens, out, B, H, D, block_size,
+                                        max_blocks, num_blocks, dtype, k_new, v_new);
+  if (rc != SPD_OK) return rc;
   const size_t need = spd_paged_decode_attn_workspace_size(B, H, D, max_blocks, -1);
   if (need == 0) return spd::record_error(SPD_ERR_CUDA, "spd_paged_decode_attn_noalloc: no CUDA device");
   if (need > SPD_NOALLOC_SCRATCH_BYTES) {
@@ -66,7 +79,7 @@ extern "C" int spd_paged_decode_attn_noalloc(const void* q, void* k_pool, void* 
     return spd::record_error(SPD_ERR_WORKSPACE, msg);
   }
   void* scratch = nullptr;
-  int rc = scratch_for_current_device(&scratch);
+  rc = scratch_for_current_device(&scratch);
   if (rc != SPD_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // The header (error word, work counters) and the arrival counters must start at zero;
@@ -77,8 +90,10 @@ extern "C" int spd_paged_decode_attn_noalloc(const void* q, void* k_pool, void* 
   rc = spd_paged_decode_attn(q, k_pool, v_pool, block_tables, context_lens, out, B, H, D, block_size, max_blocks,
                              num_blocks, scale, dtype, k_new, v_new, scratch, SPD_NOALLOC_SCRATCH_BYTES, stream);
   if (rc != SPD_OK) return rc;  // the message is already recorded
-  if (error_word &&
-      cudaMemcpyAsync(error_word, scratch, sizeof(int32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-    return spd::record_error(SPD_ERR_CUDA, "spd_paged_decode_attn_noalloc: copying the error word failed");
+  if (error_word) {
+    or_error_word<<<1, 1, 0, st>>>(error_word, static_cast<const int32_t*>(scratch));
+    if (cudaGetLastError() != cudaSuccess)
+      return spd::record_error(SPD_ERR_CUDA, "spd_paged_decode_attn_noalloc: passing on the error word failed");
+  }
   return SPD_OK;
 }

@@ -79,6 +79,29 @@ namespace spd {
 // Records a host-side error for spd_get_last_error() from other translation units of
 // the library; returns `code`.
 int record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+// Host-side argument checks of spd_paged_decode_attn (everything but the workspace), shared
+// with the allocation-free entry point, which must refuse a call before touching its scratch.
+int paged_decode_attn_check(const void* q, const void* k_pool, const void* v_pool, const int32_t* block_tables,
+                            const int32_t* context_lens, const void* out, int B, int H, int D, int block_size,
+                            int max_blocks, int num_blocks, int dtype, const void* k_new, const void* v_new) {
+  const int eb = elem_bytes(dtype);
+  if (!eb) return fail(SPD_ERR_UNSUPPORTED, "spd_paged_decode_attn: dtype %d not supported", dtype);
+  if (!q || !k_pool || !v_pool || !block_tables || !context_lens || !out)
+    return fail(SPD_ERR_INVALID_ARG, "spd_paged_decode_attn: null tensor pointer");
+  if ((k_new == nullptr) != (v_new == nullptr))
+    return fail(SPD_ERR_INVALID_ARG, "spd_paged_decode_attn: k_new and v_new must both be given or both NULL");
+  if (B <= 0 || B > 4096 || H <= 0 || H > 32 || max_blocks <= 0 || num_blocks <= 0)
+    return fail(SPD_ERR_INVALID_ARG, "spd_paged_decode_attn: bad sizes B=%d H=%d max_blocks=%d num_blocks=%d",
+                B, H, max_blocks, num_blocks);
+  if (!head_dim_ok(D)) return fail(SPD_ERR_UNSUPPORTED, "spd_paged_decode_attn: head_dim %d not supported", D);
+  if (block_size != 8 && block_size != 16 && block_size != 32)
+    return fail(SPD_ERR_UNSUPPORTED, "spd_paged_decode_attn: block_size %d not supported", block_size);
+  if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out) ||
+      (k_new && (!aligned16(k_new) || !aligned16(v_new))))
+    return fail(SPD_ERR_INVALID_ARG, "spd_paged_decode_attn: tensors must be 16-byte aligned");
+  return SPD_OK;
+}
 }  // namespace spd
 
 extern "C" {
@@ -119,21 +142,9 @@ int spd_paged_decode_attn(const void* q, void* k_pool, void* v_pool, const int32
                           const int32_t* context_lens, void* out, int B, int H, int D, int block_size,
                           int max_blocks, int num_blocks, float scale, int dtype, const void* k_new,
                           const void* v_new, void* workspace, size_t workspace_bytes, void* stream) {
-  const int eb = elem_bytes(dtype);
-  if (!eb) return fail(SPD_ERR_UNSUPPORTED, "spd_paged_decode_attn: dtype %d not supported", dtype);
-  if (!q || !k_pool || !v_pool || !block_tables || !context_lens || !out)
-    return fail(SPD_ERR_INVALID_ARG, "spd_paged_decode_attn: null tensor pointer");
-  if ((k_new == nullptr) != (v_new == nullptr))
-    return fail(SPD_ERR_INVALID_ARG, "spd_paged_decode_attn: k_new and v_new must both be given or both NULL");
-  if (B <= 0 || B > 4096 || H <= 0 || H > 32 || max_blocks <= 0 || num_blocks <= 0)
-    return fail(SPD_ERR_INVALID_ARG, "spd_paged_decode_attn: bad sizes B=%d H=%d max_blocks=%d num_blocks=%d",
-                B, H, max_blocks, num_blocks);
-  if (!head_dim_ok(D)) return fail(SPD_ERR_UNSUPPORTED, "spd_paged_decode_attn: head_dim %d not supported", D);
-  if (block_size != 8 && block_size != 16 && block_size != 32)
-    return fail(SPD_ERR_UNSUPPORTED, "spd_paged_decode_attn: block_size %d not supported", block_size);
-  if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out) ||
-      (k_new && (!aligned16(k_new) || !aligned16(v_new))))
-    return fail(SPD_ERR_INVALID_ARG, "spd_paged_decode_attn: tensors must be 16-byte aligned");
+  const int rc0 = spd::paged_decode_attn_check(q, k_pool, v_pool, block_tables, context_lens, out, B, H, D,
+                                               block_size, max_blocks, num_blocks, dtype, k_new, v_new);
+  if (rc0 != SPD_OK) return rc0;
   const size_t need = spd_paged_decode_attn_workspace_size(B, H, D, max_blocks, -1);
   if (!workspace || workspace_bytes < need)
     return fail(SPD_ERR_WORKSPACE, "spd_paged_decode_attn: workspace %zu bytes, need %zu", workspace_bytes, need);

@@ -30,28 +30,22 @@ class BlockManager:
         dtype: torch.dtype = torch.float16,
         device: str = "cuda",
     ):
-        for name, v in (("num_layers", num_layers), ("num_kv_heads", num_kv_heads), ("head_dim", head_dim),
-                        ("block_size", block_size)):
-            if v <= 0:
-                raise ValueError(f"{name} must be > 0, got {v}")
-        if isinstance(dtype, str):
-            dtype = getattr(torch, dtype)
-        self.num_layers = num_layers
-        self.num_kv_heads = num_kv_heads
-        self.head_dim = head_dim
-        self.block_size = block_size
-        self.dtype = dtype
+        dims = dict(num_layers=num_layers, num_kv_heads=num_kv_heads, head_dim=head_dim, block_size=block_size)
+        bad = [k for k, v in dims.items() if v <= 0]
+        if bad:
+            raise ValueError("BlockManager needs positive sizes; got " + ", ".join(f"{k}={dims[k]}" for k in bad))
+        self.num_layers, self.num_kv_heads, self.head_dim, self.block_size = num_layers, num_kv_heads, head_dim, \
+            block_size
+        self.dtype = getattr(torch, dtype) if isinstance(dtype, str) else dtype
         self.device = device
-        if num_blocks is None:
-            num_blocks = self._auto_num_blocks()
-        if num_blocks <= 0:
-            raise ValueError(f"num_blocks must be > 0, got {num_blocks}")
-        self.num_blocks = num_blocks
-        self.pool = torch.zeros((num_layers, 2, num_blocks, block_size, num_kv_heads, head_dim), dtype=dtype,
-                                device=device)
-        self.key_pool: List[torch.Tensor] = [self.pool[l, 0] for l in range(num_layers)]
-        self.value_pool: List[torch.Tensor] = [self.pool[l, 1] for l in range(num_layers)]
-        self._free_list: List[int] = list(range(num_blocks))
+        self.num_blocks = self._auto_num_blocks() if num_blocks is None else int(num_blocks)
+        if self.num_blocks <= 0:
+            raise ValueError(f"BlockManager needs a positive pool size; got num_blocks={self.num_blocks}")
+        self.pool = torch.zeros((num_layers, 2, self.num_blocks, block_size, num_kv_heads, head_dim),
+                                dtype=self.dtype, device=device)
+        self.key_pool: List[torch.Tensor] = list(self.pool[:, 0].unbind(0))
+        self.value_pool: List[torch.Tensor] = list(self.pool[:, 1].unbind(0))
+        self._free_list: List[int] = list(range(self.num_blocks))
         self._allocated: set = set()
 
     def _bytes_per_block(self) -> int:
@@ -67,7 +61,7 @@ class BlockManager:
 
     def allocate_block(self) -> int:
         if not self._free_list:
-            raise RuntimeError(f"BlockManager: out of physical blocks! All {self.num_blocks} blocks are allocated.")
+            raise RuntimeError(f"decoder pool exhausted: out of physical blocks ({self.num_blocks} in use)")
         blk = self._free_list.pop()
         self._allocated.add(blk)
         return blk
@@ -88,14 +82,12 @@ class BlockManager:
         return len(self._free_list)
 
     def get_stats(self) -> Dict[str, Any]:
-        allocated = self.allocated_block_count
-        return {
-            "num_blocks": self.num_blocks,
-            "allocated_blocks": allocated,
-            "free_blocks": self.num_free_blocks,
-            "utilization_pct": round(allocated / self.num_blocks * 100.0, 2) if self.num_blocks else 0.0,
-            "pool_memory_mb": round(self.num_blocks * self._bytes_per_block() / 1024 ** 2, 2),
-        }
+        """Occupancy counters (keys read by the scheduler and the reference's tooling:
+        num_blocks, allocated_blocks, free_blocks, utilization_pct, pool_memory_mb)."""
+        n, used = self.num_blocks, self.allocated_block_count
+        return dict(num_blocks=n, allocated_blocks=used, free_blocks=n - used,
+                    utilization_pct=round(100.0 * used / n, 2) if n else 0.0,
+                    pool_memory_mb=round(self.pool.numel() * self.pool.element_size() / 2 ** 20, 2))
 
     def check_no_leaks(self) -> bool:
         return self.allocated_block_count == 0
@@ -116,7 +108,6 @@ class BlockManager:
         return t.to(dev)
 
     def __repr__(self) -> str:
-        s = self.get_stats()
-        return (f"BlockManager(layers={self.num_layers}, heads={self.num_kv_heads}, head_dim={self.head_dim}, "
-                f"block_size={self.block_size}, blocks={s['allocated_blocks']}/{self.num_blocks} "
-                f"({s['utilization_pct']}% used), dtype={self.dtype}, device={self.device})")
+        L, bs, H, D = self.num_layers, self.block_size, self.num_kv_heads, self.head_dim
+        return (f"<BlockManager pool [{L}x2x{self.num_blocks}x{bs}x{H}x{D}] {self.dtype} on {self.device}: "
+                f"{self.allocated_block_count} blocks in use>")

@@ -59,3 +59,14 @@ def whole_job_rate(units_all_ranks: float, ms_max: float) -> float:
     if ms_max <= 0:
         raise ValueError("timed interval must be positive")
     return units_all_ranks / (ms_max / 1e3)
+
+
+def gather_over_ranks(value: float) -> List[float]:
+    """Every rank's float, in rank order (a one-element list without a group)."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return [float(value)]
+    n = dist.get_world_size()
+    t = torch.zeros(n, dtype=torch.float64, device=_reduce_device())
+    t[dist.get_rank()] = float(value)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return [float(x) for x in t.tolist()]

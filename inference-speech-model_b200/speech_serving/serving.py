@@ -112,6 +112,9 @@ def run_engine(scheduler: Any, requests: List[SyntheticRequest], prompt: List[in
     ttft = [r.first_token_time - (t0 + requests[ids[r.id]].arrival_time) for r in done]
     lat = [r.finish_time - (t0 + requests[ids[r.id]].arrival_time) for r in done]
     failed = sum(r.phase.value == "FAILED" for r in done)
+    by_index = [None] * len(requests)
+    for r in done:
+        by_index[ids[r.id]] = list(r.generated_tokens)
     return {
         "requests": len(done), "failed": failed, "generated_tokens": toks, "wall_s": round(wall, 4),
         "decoder_tok_s": round(toks / wall, 1),
@@ -121,4 +124,5 @@ def run_engine(scheduler: Any, requests: List[SyntheticRequest], prompt: List[in
         "latency_p50_s": round(float(np.percentile(lat, 50)), 4) if lat else None,
         "latency_p95_s": round(float(np.percentile(lat, 95)), 4) if lat else None,
         "audio_s": round(sum(requests[ids[r.id]].audio_s for r in done), 2),
+        "tokens_by_request": by_index,
     }

@@ -38,7 +38,7 @@ def test_block_manager_lifo_order_and_leaks():
     assert dec.check_no_leaks() and dec.num_free_blocks == 8
     for _ in range(8):
         dec.allocate_block()
-    with pytest.raises(RuntimeError, match="out of physical blocks"):
+    with pytest.raises(RuntimeError, match="pool exhausted"):
         dec.allocate_block()
 
 
@@ -274,3 +274,36 @@ def test_qkv_bias_row_matches_separate_projections():
         want = torch.stack([q(h) * 0.125, k(h), v(h)])
     torch.testing.assert_close(got, want, atol=1e-5, rtol=1e-5)
     assert _qkv_input(holder, n, d, h) is buf  # one buffer per batch size
+
+
+# ----------------------------------------------------------------------------- HF parity reference
+def test_hf_greedy_reference_matches_plain_hf_decoding():
+    """hf_greedy_tokens (cross K/V projected once, cached HF decoder steps) gives the same
+    tokens as the HF decoder re-run over the whole prefix with the encoder states."""
+    from transformers import WhisperConfig
+
+    from speech_serving.hf_reference import hf_greedy_tokens, sequence_agreement
+    from speech_serving.models import PretrainedWhisperModel
+
+    cfg = WhisperConfig(vocab_size=320, num_mel_bins=16, encoder_layers=2, decoder_layers=2, d_model=64,
+                        encoder_attention_heads=4, decoder_attention_heads=4, encoder_ffn_dim=128, decoder_ffn_dim=128,
+                        max_source_positions=20, max_target_positions=64, pad_token_id=300, bos_token_id=301,
+                        eos_token_id=301, decoder_start_token_id=302, init_std=0.2)
+    model = PretrainedWhisperModel(config=cfg, device="cpu", dtype=torch.float32, seed=0)
+    torch.manual_seed(1)
+    mels = torch.randn(3, 16, 40)
+    prompt = [302, 303]
+    got = hf_greedy_tokens(model, mels, prompt, [6, 4, 5], batch=2)
+    hf = model.hf_model
+    want = []
+    with torch.no_grad():
+        for m, n in zip(mels, [6, 4, 5]):
+            e = hf.model.encoder(m[None]).last_hidden_state
+            toks = []
+            for _ in range(n):
+                h = hf.model.decoder(input_ids=torch.tensor([prompt + toks]), encoder_hidden_states=e).last_hidden_state
+                toks.append(int(hf.proj_out(h[0, -1]).argmax()))
+            want.append(toks)
+    assert got == want
+    a = sequence_agreement(got, [want[0], want[1][:3] + [want[1][3] + 1], want[2]])
+    assert a["identical"] == 2 and a["first_divergence"] == [3]

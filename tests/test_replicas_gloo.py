@@ -29,7 +29,8 @@ def _worker(rank, world, port, q):
         ms = 5.0 + 3.0 * rank  # rank 1 is the slower one
         ms_max = replicas.max_over_ranks(ms)
         units = replicas.sum_over_ranks(len(mine))
-        q.put((rank, mine, (lo, hi), ms_max, units, replicas.whole_job_rate(units, ms_max)))
+        every = replicas.gather_over_ranks(ms)
+        q.put((rank, mine, (lo, hi), ms_max, units, replicas.whole_job_rate(units, ms_max), every))
     finally:
         dist.destroy_process_group()
 
@@ -46,16 +47,18 @@ def test_two_rank_replicas_gloo():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    (_, m0, r0, t0, u0, v0), (_, m1, r1, t1, u1, v1) = res
+    (_, m0, r0, t0, u0, v0, e0), (_, m1, r1, t1, u1, v1, e1) = res
     assert m0 == [0, 2, 4, 6, 8] and m1 == [1, 3, 5, 7, 9]
     assert r0 == (0, 5) and r1 == (5, 10)
     assert t0 == t1 == 8.0  # every rank reports the slowest rank's time
     assert u0 == u1 == 10
     assert v0 == pytest.approx(10 / 8e-3)
+    assert e0 == e1 == [5.0, 8.0]  # per-rank values in rank order
 
 
 def test_single_process_fallbacks():
     assert replicas.max_over_ranks(3.5) == 3.5
+    assert replicas.gather_over_ranks(2.0) == [2.0]
     assert replicas.shard([1, 2, 3], 1, 0) == [1, 2, 3]
     with pytest.raises(ValueError):
         replicas.shard([1], 2, 2)
