@@ -84,6 +84,22 @@ int spd_get_last_error(char* buf, size_t size);
 size_t spd_paged_decode_attn_workspace_size(int B, int H, int D, int max_blocks, int device);
 size_t spd_cross_attn_workspace_size(int B, int H, int D, int device);
 
+/* Bound on every wait of the attention kernels (spd_paged_decode_attn, its allocation-free
+ * variant, spd_cross_attn) launched by the calling thread from now on; each launch takes
+ * the value as a kernel parameter.  A wait that runs out records SPD_DEVERR_TIMEOUT in the
+ * error word, the launch stops its work (outputs are then undefined), waits for its own
+ * copies in flight and returns; the context stays usable.  0 restores the default of 2 s
+ * (SPD_DEFAULT_WAIT_NS).  No counterpart in the reference, whose kernels never wait. */
+#define SPD_DEFAULT_WAIT_NS 2000000000ull
+int spd_set_wait_timeout_ns(uint64_t ns);
+uint64_t spd_get_wait_timeout_ns(void);
+
+/* Exercises the bounded-wait path on the GPU: one CTA waits on a shared-memory barrier
+ * phase that nothing completes, gives up after timeout_ns (0 < timeout_ns <= 2 s) and
+ * ORs SPD_DEVERR_TIMEOUT into *error_word.  Issues no copy; faults and hangs nothing.
+ * For failure-detection tests; no counterpart in the reference. */
+int spd_selftest_wait_timeout(int32_t* error_word, uint64_t timeout_ns, void* stream);
+
 /* Copies the device error word of a workspace (or any int32 error word) to *host_word.
  * Synchronises `stream`. Not for use during graph capture. */
 int spd_read_error_word(const void* error_word, int32_t* host_word, void* stream);

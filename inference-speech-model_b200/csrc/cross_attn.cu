@@ -116,7 +116,8 @@ __global__ void __launch_bounds__(288) cross_attn_kernel(const CrossParams p) {
   auto issue_item = [&](int b, int h, int k, int v, int nch) {
     const int j0 = k * N, j1 = min(j0 + N, nch);
     for (int j = j0; j < j1; ++j) {
-      if (n_issued >= S && (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&empty[s_p], ph_p ^ 1, p.err))) {
+      if (n_issued >= S &&
+          (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&empty[s_p], ph_p ^ 1, p.err, p.wait_ns))) {
         flag[0] = 1;
         alive = false;
         return;
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(288) cross_attn_kernel(const CrossParams p) {
         q = nxt;
       }
       // end-of-work stage for the compute warps
-      if (alive && n_issued >= S && !mbar_wait_bounded(&empty[s_p], ph_p ^ 1, p.err)) alive = false;
+      if (alive && n_issued >= S && !mbar_wait_bounded(&empty[s_p], ph_p ^ 1, p.err, p.wait_ns)) alive = false;
       if (alive) {
         meta[s_p] = CrossStage{-1, 0, 0, 0, 0, 0, 0, 0};
         mbar_arrive(&full[s_p]);
@@ -251,7 +252,7 @@ __global__ void __launch_bounds__(288) cross_attn_kernel(const CrossParams p) {
   uint32_t ph = 0;
 
   for (;;) {
-    if (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&full[s], ph, p.err)) {
+    if (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&full[s], ph, p.err, p.wait_ns)) {
       flag[0] = 1;
       break;
     }

@@ -151,6 +151,10 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
   using Gm = PagedGeom<T, D, BS>;
   constexpr int LPR = Gm::LPR, DPL = Gm::DPL, CH = Gm::CH, NCH = Gm::NCH;
   constexpr int VE = Gm::VE, CPR = Gm::CPR, RG = Gm::RG, PVP = Gm::PVP;
+  // q·k on the tensor cores (mma m16n8k16): 16-bit types, 16-row blocks, D of 64 or 128
+  // (enough 8-element chunks per row for a conflict-free rotation over 8 rows)
+  constexpr bool kMma = sizeof(T) == 2 && BS == 16 && (D == 64 || D == 128);
+  static_assert(!kMma || (RG * PVP == BS && (8 % RG) == 0), "p·v row groups split at row 8");
 
   extern __shared__ __align__(128) unsigned char smem[];
   const int H = p.H, B = p.B, S = p.stages, MB = p.max_blocks;
@@ -171,8 +175,9 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
   StageMeta* meta = reinterpret_cast<StageMeta*>(setup + 2);  // 16-byte aligned
   int* flag = reinterpret_cast<int*>(meta + S);               // [0] abort, [1..3] spare
   int* ctx_s = flag + 4;                                      // [round4(B)] context lengths
-  int* ip = ctx_s + ((B + 3) & ~3);                           // [B + 1] queued-chunk prefix
-  int* tab_s = ip + ((B + 4) & ~3);                           // [B * MB] block table copy
+  int* ip = ctx_s + ((B + 3) & ~3);                           // [B + 1] prefix of queued full chunks
+  int* ipp = ip + ((B + 4) & ~3);                             // [B + 1] prefix of queued partial chunks
+  int* tab_s = ipp + ((B + 4) & ~3);                          // [B * MB] block table copy
   const bool tab_in_smem = p.table_in_smem != 0;
 
   int* next_item = p.work + 0;  // queue counter
@@ -198,8 +203,45 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
   __syncthreads();
   // Launched with programmatic dependent launch: this grid may become resident while the
   // previous kernel in the stream still runs, so every thread waits for it before reading
-  // an input or writing an output.  Then the merge kernel that follows may get resident
-  // early; it waits for this grid to finish (griddepcontrol.wait) before reading anything.
+  // an input for use or writing an output.  Then the merge kernel that follows may get
+  // resident early; it waits for this grid to finish (griddepcontrol.wait) before reading
+  // anything.
+  //
+  // Before the wait, one compute warp only warms L2 (the producer goes straight to the
+  // wait): it reads, bypassing L1, the length and block ids of this CTA's first chunk,
+  // which the previous kernel may still be writing, and prefetches those blocks' K/V rows,
+  // the lengths and the block table into L2.  A stale value only wastes a prefetch (block
+  // ids are clamped into the pool); the rows are copied, and every input is read again,
+  // after the wait.  So the DRAM fetch of every CTA's first chunk overlaps the previous
+  // kernel's tail.
+  if (warp == NW - 1 && lane == 0) {
+    const int b0 = (int)blockIdx.x % B, c0 = (int)blockIdx.x / B;
+    if (c0 < MC) {
+      int phys[kItemUnits];
+      const int ctx_raw = __ldcg(p.context_lens + b0);
+#pragma unroll
+      for (int u = 0; u < kItemUnits; ++u) {
+        const int j = min(c0 * kItemUnits + u, MB - 1);
+        phys[u] = __ldcg(p.block_tables + (size_t)b0 * MB + j);
+      }
+      const int ctx0 = clamp_ctx(ctx_raw, max_ctx);
+      const uint32_t row_bytes = (uint32_t)(HD * (int)sizeof(T));
+#pragma unroll
+      for (int u = 0; u < kItemUnits; ++u) {
+        const int j = c0 * kItemUnits + u;
+        const int rows = min(BS, ctx0 - j * BS);
+        if (j >= MB || rows <= 0) break;
+        const int ph = phys[u] < 0 ? 0 : (phys[u] >= p.num_blocks ? p.num_blocks - 1 : phys[u]);
+        bulk_prefetch_l2(kpool + (size_t)ph * unit_elems, (uint32_t)rows * row_bytes);
+        bulk_prefetch_l2(vpool + (size_t)ph * unit_elems, (uint32_t)rows * row_bytes);
+      }
+    }
+    if (blockIdx.x == 0) {
+      if ((B * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.context_lens) & 15) == 0)
+        bulk_prefetch_l2(p.context_lens, (uint32_t)B * 4u);
+      if (tab_in_smem) bulk_prefetch_l2(p.block_tables, (uint32_t)B * MB * 4u);
+    }
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0) SPD_TRACE(6);
@@ -207,8 +249,13 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
   // ---- 2. producer warp --------------------------------------------------------------
   // Work: chunk c of sequence b (blocks [c*kItemUnits, (c+1)*kItemUnits)) is one item.
   // CTA g starts on chunk g / B of sequence g % B, located with direct loads so that its
-  // copies start one round trip after the wait; the other chunks form a queue (sequence-
-  // major) handed out by a global counter once the lengths have arrived.
+  // copies start one round trip after the wait; the other chunks form a queue handed out
+  // by a global counter once the lengths have arrived: first every chunk whose rows are
+  // all valid (sequence-major), then the shorter last chunks, so the final items handed
+  // out are the small ones.  While more than a grid's worth of items is left, the next
+  // item is taken one step ahead (hiding the atomic's latency); near the end it is taken
+  // only once the current item's copies are issued, so no CTA sits on an item it cannot
+  // start yet.
   if (warp == NW) {
     const uint64_t pol = l2_policy_evict_first();
     int s = 0;
@@ -218,7 +265,8 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
     const uint32_t row_bytes = (uint32_t)(HD * (int)sizeof(T));
     // stages the unit j of item (b, chunk) (lane 0 only)
     auto issue_unit = [&](int b, int j, int ctx, int phys, int chunk, int nch, bool first, bool last) {
-      if (n_issued >= S && (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&empty[s], ph ^ 1, p.err))) {
+      if (n_issued >= S &&
+          (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&empty[s], ph ^ 1, p.err, p.wait_ns))) {
         flag[0] = 1;
         alive = false;
         return;
@@ -306,15 +354,15 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
     __syncwarp();
     // lengths: clamp, chunks per sequence, and the prefix of each sequence's queued chunks
     // (its chunks minus the ones CTAs started on)
-    if (!mbar_wait_bounded(setup, 0, p.err)) flag[0] = 1;
+    if (!mbar_wait_bounded(setup, 0, p.err, p.wait_ns)) flag[0] = 1;
     if (!ctx_bulk)
       for (int i = lane; i < B; i += 32) ctx_s[i] = p.context_lens[i];
     __syncwarp();
     {
-      int carry = 0;
+      int carry = 0, carryp = 0;
       for (int base = 0; base < B; base += 32) {
         const int i = base + lane;
-        int v = 0;
+        int v = 0, vp = 0;
         if (i < B) {
           const int c0 = ctx_s[i];
           if (c0 > max_ctx) set_error(p.err, SPD_DEVERR_LENGTH);
@@ -322,17 +370,29 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
           ctx_s[i] = c;
           const int nch = ((c + BS - 1) / BS + kItemUnits - 1) / kItemUnits;
           const int started = i < G ? min((G - 1 - i) / B + 1, nch) : 0;
-          v = nch - started;
+          // the last chunk is "partial" when it has fewer than kItemUnits * BS rows; it
+          // joins the queue's second phase unless a CTA started on it
+          const int part = (c % (kItemUnits * BS) != 0 && nch - 1 >= started) ? 1 : 0;
+          v = nch - started - part;
+          vp = part;
         }
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const int n = __shfl_up_sync(0xffffffffu, v, o);
-          if (lane >= o) v += n;
+          const int np = __shfl_up_sync(0xffffffffu, vp, o);
+          if (lane >= o) {
+            v += n;
+            vp += np;
+          }
         }
-        if (i < B) ip[i + 1] = v + carry;
+        if (i < B) {
+          ip[i + 1] = v + carry;
+          ipp[i + 1] = vp + carryp;
+        }
         carry += __shfl_sync(0xffffffffu, v, 31);
+        carryp += __shfl_sync(0xffffffffu, vp, 31);
       }
-      if (lane == 0) ip[0] = 0;
+      if (lane == 0) ip[0] = ipp[0] = 0;
     }
     __syncwarp();
     if (lane == 0) SPD_TRACE(1);
@@ -341,26 +401,35 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
       if (ctx_s[b] == 0)
         for (int i = lane; i < HD; i += 32) out[(size_t)b * HD + i] = Elem<T>::from_f(0.f);
     if (lane == 0) {
-      const int n_queue = ip[B];
+      const int n_full = ip[B];
+      const int n_queue = n_full + ipp[B];
       alive = alive && !flag[0];
       while (alive && q < n_queue) {
-        const int nxt = atomicAdd(next_item, 1);  // next take, in flight meanwhile
-        const int b = upper_index_i32(ip, B, q);
+        const bool ahead = n_queue - q > G;
+        int nxt = ahead ? atomicAdd(next_item, 1) : 0;  // next take, in flight meanwhile
+        int b, c;
+        const bool full_phase = q < n_full;
+        b = full_phase ? upper_index_i32(ip, B, q) : upper_index_i32(ipp, B, q - n_full);
         const int ctx = ctx_s[b];
         const int nblk = (ctx + BS - 1) / BS;
         const int nch = (nblk + kItemUnits - 1) / kItemUnits;
-        const int started = b < G ? min((G - 1 - b) / B + 1, nch) : 0;
-        const int c = started + (q - ip[b]);
+        if (full_phase) {
+          const int started = b < G ? min((G - 1 - b) / B + 1, nch) : 0;
+          c = started + (q - ip[b]);
+        } else {
+          c = nch - 1;
+        }
         const int j0 = c * kItemUnits, j1 = min(j0 + kItemUnits, nblk);
         for (int j = j0; j < j1 && alive; ++j) {
           const int phys = tab_in_smem ? tab_s[b * MB + j] : p.block_tables[(size_t)b * MB + j];
           issue_unit(b, j, ctx, phys, c, nch, j == j0, j == j1 - 1);
         }
+        if (!ahead) nxt = atomicAdd(next_item, 1);
         q = nxt;
       }
       SPD_TRACE(3);
       // end-of-work stage for the compute warps
-      if (alive && n_issued >= S && !mbar_wait_bounded(&empty[s], ph ^ 1, p.err)) alive = false;
+      if (alive && n_issued >= S && !mbar_wait_bounded(&empty[s], ph ^ 1, p.err, p.wait_ns)) alive = false;
       if (alive) {
         meta[s] = StageMeta{-1, 0, 0, 0, 0, 0, 0, 0};
         mbar_arrive(&full[s]);
@@ -382,6 +451,7 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
           const long long u = n_issued - 1 - k;
           (void)mbar_wait_bounded(&full[u % S], (uint32_t)((u / S) & 1), nullptr);
         }
+        (void)mbar_wait_bounded(setup, 0, nullptr);  // the lengths / table copies
       }
       SPD_TRACE(7);
     }
@@ -394,15 +464,18 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
   const int rot = r & (NCH - 1);
   const int cidx = lane % CPR;  // p·v chunk of this lane
   const int rg = lane / CPR;    // p·v row group
+  // tensor-core q·k (16-bit types, 16-row blocks, D = 64 or 128): fragment coordinates
+  const int fg = lane >> 2, fc = lane & 3;
 
-  float2 qr[HPW][DPL / 2];
+  float2 qr[HPW][kMma ? 1 : DPL / 2];
+  uint32_t qb[HPW][kMma ? D / 8 : 1];
   float m[HPW], l[HPW];
   float2 acc[HPW][VE / 2];
   int s = 0;
   uint32_t ph = 0;
   bool traced = false;
   for (;;) {
-    if (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&full[s], ph, p.err)) {
+    if (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&full[s], ph, p.err, p.wait_ns)) {
       flag[0] = 1;
       return;
     }
@@ -427,11 +500,22 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
 #pragma unroll
         for (int i = 0; i < VE / 2; ++i) acc[k][i] = make_float2(0.f, 0.f);
         if (h < H) {
-          const T* qrow = Qs + h * D + sub * DPL;
+          if constexpr (kMma) {
+            // B fragments of q: column n of k-step j holds q's 8-element chunks
+            // (2j + n) and (2j + 1 + n) mod D/8 (see the q·k comment below)
+            const T* qrow = Qs + h * D;
 #pragma unroll
-          for (int cc = 0; cc < NCH; ++cc) {
-            const int ci = (cc + rot) & (NCH - 1);
-            load_f2<T, CH>(qrow + ci * CH, &qr[k][cc * CH / 2]);  // the score is scaled instead
+            for (int j = 0; j < D / 16; ++j) {
+              qb[k][2 * j] = lds_u32(qrow + ((2 * j + fg) & (D / 8 - 1)) * 8 + 2 * fc);
+              qb[k][2 * j + 1] = lds_u32(qrow + ((2 * j + 1 + fg) & (D / 8 - 1)) * 8 + 2 * fc);
+            }
+          } else {
+            const T* qrow = Qs + h * D + sub * DPL;
+#pragma unroll
+            for (int cc = 0; cc < NCH; ++cc) {
+              const int ci = (cc + rot) & (NCH - 1);
+              load_f2<T, CH>(qrow + ci * CH, &qr[k][cc * CH / 2]);  // the score is scaled instead
+            }
           }
         }
       }
@@ -475,6 +559,53 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
         if (h >= H) continue;
         const T* Kh = Ks + h * D;
         const T* Vh = Vs + h * D;
+        if constexpr (kMma) {
+          // q·k of the block's 16 rows as one m16n8k16 MMA chain: A = the K rows (row m,
+          // D in k-steps of 16), B = q.  Every 8-element chunk of a row sits at the same
+          // bank offset in every row (the row stride is a multiple of 128 bytes), so row
+          // m reads its chunks in an order rotated by m mod 8 — its k-step j covers chunks
+          // (2j + m) and (2j + 1 + m) mod D/8 — and B column n carries q's chunks in the
+          // order rotated by n.  The 8 rows of a fragment load then hit 8 different bank
+          // groups, and D[m][m mod 8] is row m's full dot product: row g's and row g+8's
+          // scores end up in lane 4g + g/2 (element g & 1 of each row pair).
+          float d[4] = {0.f, 0.f, 0.f, 0.f};
+          const T* k0 = Kh + (size_t)fg * HD;
+          const T* k1 = k0 + (size_t)8 * HD;
+#pragma unroll
+          for (int j = 0; j < D / 16; ++j) {
+            const int lo = ((2 * j + fg) & (D / 8 - 1)) * 8 + 2 * fc;
+            const int hi = ((2 * j + 1 + fg) & (D / 8 - 1)) * 8 + 2 * fc;
+            mma_16816<T>(d, lds_u32(k0 + lo), lds_u32(k1 + lo), lds_u32(k0 + hi), lds_u32(k1 + hi), qb[k][2 * j],
+                         qb[k][2 * j + 1]);
+          }
+          const bool owner = fc == (fg >> 1);
+          const float sa = (fg & 1) ? d[1] : d[0];  // row fg
+          const float sb = (fg & 1) ? d[3] : d[2];  // row fg + 8
+          const float s0 = (owner && (FULL || fg < nvalid)) ? sa * p.scale_log2 : -INFINITY;
+          const float s1 = (owner && (FULL || fg + 8 < nvalid)) ? sb * p.scale_log2 : -INFINITY;
+          const float mnew = fmaxf(m[k], warp_max_redux(fmaxf(s0, s1)));
+          const float alpha = ex2_approx(m[k] - mnew);
+          const float p0 = ex2_approx(s0 - mnew), p1 = ex2_approx(s1 - mnew);  // 0 off the owners
+          l[k] = l[k] * alpha + (p0 + p1);
+          m[k] = mnew;
+          const float2 a2 = make_float2(alpha, alpha);
+#pragma unroll
+          for (int i = 0; i < VE / 2; ++i) acc[k][i] = __fmul2_rn(acc[k][i], a2);
+#pragma unroll
+          for (int ps = 0; ps < PVP; ++ps) {
+            const int rr = ps * RG + rg;
+            const int src = 4 * (rr & 7) + ((rr & 7) >> 1);  // the lane holding row rr's weight
+            const float prr = __shfl_sync(0xffffffffu, ps * RG < 8 ? p0 : p1, src);
+            if ((FULL && rr < BS) || rr < nvalid) {
+              float2 vv[VE / 2];
+              load_f2<T, VE>(Vh + (size_t)rr * HD + cidx * VE, vv);
+              const float2 p2 = make_float2(prr, prr);
+#pragma unroll
+              for (int i = 0; i < VE / 2; ++i) acc[k][i] = __ffma2_rn(p2, vv[i], acc[k][i]);
+            }
+          }
+          continue;
+        }
         const bool rv = FULL || r < nvalid;
         float sc = 0.f;
         if (rv) {
@@ -602,21 +733,27 @@ __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
   const size_t stride = (size_t)p.H * kPartialRow<D>;  // next item, same head
   T* orow = reinterpret_cast<T*>(p.out) + ((size_t)b * p.H + h) * D;
   if (nitems <= MAXI) {
-    // lane l holds elements [l*EPL, (l+1)*EPL) of every item's acc: one vector load per item
-    float2 ml = make_float2(-INFINITY, 0.f);
-    if (lane < nitems) ml = __ldcg(reinterpret_cast<const float2*>(base + lane * stride + D));
-    const bool hold = lane < D / EPL;
+    // Every lane loads every item's (m, l) (the same addresses across the warp) and its own
+    // EPL elements of every item's acc, all in one round of loads; the weights are then
+    // computed lane-locally, without shuffles.
+    float2 ml[MAXI];
     V a[MAXI];
+    const bool hold = lane < D / EPL;
 #pragma unroll
-    for (int it = 0; it < MAXI; ++it)
+    for (int it = 0; it < MAXI; ++it) {
+      ml[it] = it < nitems ? __ldcg(reinterpret_cast<const float2*>(base + it * stride + D))
+                           : make_float2(-INFINITY, 0.f);
       a[it] = (it < nitems && hold) ? __ldcg(reinterpret_cast<const V*>(base + it * stride) + lane) : V{};
-    const float M = warp_max(ml.x);
-    const float w = lane < nitems ? exp2f(ml.x - M) : 0.f;
-    const float inv = 1.f / warp_sum(ml.y * w);
+    }
+    float M = ml[0].x;
+#pragma unroll
+    for (int it = 1; it < MAXI; ++it) M = fmaxf(M, ml[it].x);
+    float L = 0.f;
     V o{};
 #pragma unroll
     for (int it = 0; it < MAXI; ++it) {
-      const float wi = __shfl_sync(0xffffffffu, w, it);
+      const float wi = ex2_approx(ml[it].x - M);  // 0 for the unused items (m = -inf)
+      L = fmaf(wi, ml[it].y, L);
       o.x = fmaf(wi, a[it].x, o.x);
       o.y = fmaf(wi, a[it].y, o.y);
       if constexpr (EPL == 4) {
@@ -624,6 +761,7 @@ __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
         o.w = fmaf(wi, a[it].w, o.w);
       }
     }
+    const float inv = 1.f / L;
     if (hold) {
       T* dst = orow + lane * EPL;
       dst[0] = Elem<T>::from_f(o.x * inv);
@@ -683,7 +821,7 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
                      (reinterpret_cast<uintptr_t>(p.block_tables) & 15) == 0)
                         ? 1
                         : 0;
-  const size_t fixed = 16 * 8 /*barriers*/ + 32 * 8 /*meta*/ + 16 + 4 * ((size_t)p.B + 4) * 2 +
+  const size_t fixed = 16 * 8 /*barriers*/ + 32 * 8 /*meta*/ + 16 + 4 * ((size_t)p.B + 4) * 3 +
                        (p.table_in_smem ? tab_bytes : 0) + 256;
   // Ring depth: up to ~216 KB per CTA (one CTA per SM at the Whisper shapes; the
   // producer warp keeps every stage in flight), at least two stages.
@@ -693,7 +831,7 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
   S = S < 1 ? 1 : (S > 8 ? 8 : S);
   p.stages = S;
   const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * ((size_t)S * 2 + 2) + 32 * (size_t)S + 16 +
-                      4 * ((((size_t)p.B + 3) & ~(size_t)3) + (((size_t)p.B + 4) & ~(size_t)3)) +
+                      4 * ((((size_t)p.B + 3) & ~(size_t)3) + 2 * (((size_t)p.B + 4) & ~(size_t)3)) +
                       (p.table_in_smem ? tab_bytes : 0);
   if (smem > (PAIR ? 113 : 227) * 1024) return SPD_ERR_UNSUPPORTED;
   auto kfn = paged_decode_attn_kernel<T, D, BS, HPW, PAIR>;

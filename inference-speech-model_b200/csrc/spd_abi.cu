@@ -27,6 +27,8 @@ namespace {
 
 thread_local char g_err_msg[512] = {0};
 thread_local int g_err_code = SPD_OK;
+// Bound on the attention kernels' waits for launches made by this thread.
+thread_local unsigned long long g_wait_ns = spd::SPD_WAIT_NS;
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -104,9 +106,41 @@ int paged_decode_attn_check(const void* q, const void* k_pool, const void* v_poo
 }
 }  // namespace spd
 
+namespace {
+// An mbarrier phase that never completes (it expects 16 bytes that no copy delivers):
+// the bounded wait must give up after limit_ns, record SPD_DEVERR_TIMEOUT and return.
+// No asynchronous operation is ever issued, so the CTA exits with nothing in flight.
+__global__ void wait_timeout_probe_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    spd::mbar_init(&bar, 1);
+    spd::fence_barrier_init();
+    spd::mbar_arrive_expect_tx(&bar, 16);
+    (void)spd::mbar_wait_bounded(&bar, 0, err, limit_ns);
+  }
+}
+}  // namespace
+
 extern "C" {
 
 int spd_version(void) { return 100; }
+
+int spd_set_wait_timeout_ns(uint64_t ns) {
+  g_wait_ns = ns ? (unsigned long long)ns : spd::SPD_WAIT_NS;
+  return ok();
+}
+
+uint64_t spd_get_wait_timeout_ns(void) { return g_wait_ns; }
+
+int spd_selftest_wait_timeout(int32_t* error_word, uint64_t timeout_ns, void* stream) {
+  if (!error_word || timeout_ns == 0 || timeout_ns > spd::SPD_WAIT_NS)
+    return fail(SPD_ERR_INVALID_ARG, "spd_selftest_wait_timeout: error_word and 0 < timeout_ns <= %llu needed",
+                (unsigned long long)spd::SPD_WAIT_NS);
+  wait_timeout_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(reinterpret_cast<int*>(error_word),
+                                                                            (unsigned long long)timeout_ns);
+  if (cudaGetLastError() != cudaSuccess) return fail(SPD_ERR_CUDA, "spd_selftest_wait_timeout: launch failed");
+  return ok();
+}
 
 int spd_get_last_error(char* buf, size_t size) {
   if (buf && size) {
@@ -156,6 +190,7 @@ int spd_paged_decode_attn(const void* q, void* k_pool, void* v_pool, const int32
   p.context_lens = context_lens; p.out = out; p.k_new = k_new; p.v_new = v_new;
   p.B = B; p.H = H; p.max_blocks = max_blocks; p.num_blocks = num_blocks;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.wait_ns = g_wait_ns;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   p.err = reinterpret_cast<int*>(ws);
   p.work = reinterpret_cast<int*>(ws + spd::kWsWorkOffset);
@@ -194,6 +229,7 @@ int spd_cross_attn(const void* q, const void* k, const void* v, const int32_t* v
   p.B = B; p.H = H; p.T_max = T_max;
   p.kv_batch_stride = kv_batch_stride; p.kv_head_stride = kv_head_stride;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.wait_ns = g_wait_ns;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   p.err = reinterpret_cast<int*>(ws);
   p.work = reinterpret_cast<int*>(ws + spd::kWsWorkOffset);

@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "../../include/spd_b200.h"
 
 namespace spd {
@@ -207,13 +209,17 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 
 // Waits for phase `parity` of `bar` to complete.  Returns false (and sets the
-// timeout flag) if it did not complete within SPD_WAIT_NS.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
+// timeout flag) if it did not complete within `limit_ns` (SPD_WAIT_NS by default).  The
+// attention kernels pass the launch's limit (spd_set_wait_timeout_ns) to the waits that
+// make progress; the waits that drain copies still in flight before a CTA exits keep the
+// default, so that shared memory is never released under a copy.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
+                                                  unsigned long long limit_ns = SPD_WAIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0 && global_ns() - t0 > SPD_WAIT_NS) {
+    if ((it & 63u) == 0 && global_ns() - t0 > limit_ns) {
       set_error(err, SPD_DEVERR_TIMEOUT);
       return false;
     }
@@ -228,7 +234,45 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Hint: bring [src, src + bytes) of global memory into L2 (no completion, no data
+// returned; src 16-byte aligned, bytes a multiple of 16).  Because it only warms L2, which
+// is coherent for the whole device, it is safe on addresses whose contents another kernel
+// may still be writing.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// 32-bit shared-memory load (a pair of 16-bit elements), for tensor-core fragments.
+__device__ __forceinline__ uint32_t lds_u32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// D += A·B on the tensor cores, m16n8k16, 16-bit inputs (T = __half or __nv_bfloat16),
+// fp32 accumulation; fragments in the PTX ISA's register layout for mma.m16n8k16.
+template <typename T>
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __half>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
 // ---------------------------------------------------------------- warp reductions
+// Maximum over the warp in one instruction (sm_100a redux.sync on fp32).
+__device__ __forceinline__ float warp_max_redux(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -23,6 +23,7 @@ struct PagedParams {
   float* partials;   // [B * ceil(max_blocks / kItemUnits) * H * (D + 8)]
   int stages;
   int table_in_smem;  // the whole block table is bulk-copied into shared memory
+  unsigned long long wait_ns;  // bound on each wait that makes progress
 };
 
 struct CrossParams {
@@ -39,6 +40,7 @@ struct CrossParams {
   float* partials;  // [B*H*kCrossMaxItems * (D + 2)]: one row per item
   int stages;
   int item_units;   // units (of the kernel's row chunk) per work item
+  unsigned long long wait_ns;  // bound on each wait that makes progress
 };
 
 struct AppendParams {

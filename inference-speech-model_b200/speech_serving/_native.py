@@ -46,6 +46,9 @@ _SIGNATURES = {
     "spd_cross_kv_project": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _i, _vp, _vp]),
     "spd_add_layernorm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i64, _f, _i, _vp]),
     "spd_argmax_rows": (_i, [_vp, _i, _i, _i64, _vp, _vp, _i, _vp]),
+    "spd_set_wait_timeout_ns": (_i, [C.c_uint64]),
+    "spd_get_wait_timeout_ns": (C.c_uint64, []),
+    "spd_selftest_wait_timeout": (_i, [_vp, C.c_uint64, _vp]),
     "spd_paged_decode_attn_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i, _vp, _vp,
                                            _vp, _vp]),
 }

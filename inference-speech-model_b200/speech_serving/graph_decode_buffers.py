@@ -303,6 +303,13 @@ class GraphDecodeBuffers(PagedDecodeState):
                 else:
                     s.generated_count += 1
 
+    def reset_window(self) -> None:
+        """Drops the current readback window (after a failed step: its tokens are void)."""
+        self._step_in_k = 0
+        self._window_buckets = []
+        for s in self.slots:
+            s.readback_start = 0
+
     def should_readback(self) -> bool:
         if self._step_in_k >= self.readback_k:
             return True

@@ -540,16 +540,28 @@ class PhaseAwareSpeechScheduler:
                     buf.set_table(req.slot_idx, req.decoder_block_table)
         active = list(self.active_decode)
         t0 = time.perf_counter()
-        with self.phase_timer.measure(active, "host_between_replays"):
-            bucket = buf.prepare_replay()
-        with self.phase_timer.measure(active, "graph_replay"):
-            buf.replay_step(bucket)
-        self.decode_steps += 1
-        if not buf.should_readback():
-            self.decode_time_s += time.perf_counter() - t0
+        try:
+            with self.phase_timer.measure(active, "host_between_replays"):
+                bucket = buf.prepare_replay()
+            with self.phase_timer.measure(active, "graph_replay"):
+                buf.replay_step(bucket)
+            self.decode_steps += 1
+            if not buf.should_readback():
+                self.decode_time_s += time.perf_counter() - t0
+                return
+            with self.phase_timer.measure(active, "readback_wait"):
+                results = buf.sync_tokens()
+        except Exception as e:
+            # One batched step serves every active request, so a failed step fails all of
+            # them; each is released (slot, decoder and encoder blocks) as in the reference's
+            # per-request handler (phase_aware_scheduler.py:1037-1039 there).
+            logger.error(f"decode step failed for requests {[r.id for r in active]}: {e}")
+            buf.reset_window()
+            for req in active:
+                if not req.done:
+                    self._complete_request(req, status=RequestPhase.FAILED)
+            self.active_decode = [r for r in self.active_decode if not r.done]
             return
-        with self.phase_timer.measure(active, "readback_wait"):
-            results = buf.sync_tokens()
         self.decode_time_s += time.perf_counter() - t0
         done = []
         for slot, toks in results:

@@ -11,7 +11,7 @@ from speech_serving import ops
 
 def _declared(repo):
     text = (repo / "include" / "spd_b200.h").read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|size_t)\s+(spd_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|uint64_t)\s+(spd_\w+)\s*\(", text, re.M)))
 
 
 def test_header_declares_the_bound_symbols(golden_dir):

@@ -112,6 +112,45 @@ def test_generation_stops_on_eos_eager():
     assert enc.allocated_block_count == 0 and dec.allocated_block_count == 0
 
 
+@pytest.mark.parametrize("graph", [False, True])
+def test_failed_decode_step_releases_everything(graph):
+    """A decode step that raises mid-run fails the requests it was serving, returns
+    their slots and every decoder and encoder block (the reference releases a request's
+    resources when its decode raises, phase_aware_scheduler.py:1037-1039), and the
+    scheduler goes on serving new requests."""
+    model = _model(7, vocab=256)
+    s, enc, dec = _sched(model, 64, 64, bs=8, max_batch_size=4, graph_decode=graph, graph_readback_k=2)
+    buf = s.graph_buffers
+    target = (buf, "replay_step") if graph else (model, "decode_step_paged")
+    real = getattr(*target)
+    calls = [0]
+
+    def failing(*a, **k):
+        calls[0] += 1
+        if calls[0] == 3:
+            raise RuntimeError("injected failure in the decode step")
+        return real(*a, **k)
+
+    setattr(*target, failing)
+    try:
+        for _ in range(3):
+            assert s.submit(torch.randn(80, 48, device=DEV, dtype=torch.float16), max_new_tokens=12) is not None
+        done = list(s.run_until_done())
+    finally:
+        setattr(*target, real)
+    assert len(done) == 3 and all(r.done for r in done)
+    failed = [r for r in done if r.phase == RequestPhase.FAILED]
+    assert failed, [r.phase for r in done]
+    assert enc.allocated_block_count == 0 and dec.allocated_block_count == 0
+    assert buf.active_slot_count() == 0
+    assert all(r.decoder_block_table == [] and r.encoder_block_table == [] for r in done)
+    # the scheduler still serves: a new request completes normally
+    s.submit(torch.randn(80, 48, device=DEV, dtype=torch.float16), max_new_tokens=6)
+    (r,) = [x for x in s.run_until_done() if x not in done]
+    assert r.phase == RequestPhase.COMPLETED and len(r.generated_tokens) == 6
+    assert enc.allocated_block_count == 0 and dec.allocated_block_count == 0 and buf.active_slot_count() == 0
+
+
 def test_graph_decode_eos_trims_tokens():
     model = _model(303)
     mel = torch.randn(80, 200, device=DEV, dtype=torch.float16)

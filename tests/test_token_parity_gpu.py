@@ -11,10 +11,14 @@ decoded greedily by the unpatched HF decoder (speech_serving.hf_reference, the r
 PretrainedWhisperModel arithmetic) on the same device, dtype and seeded random-init
 weights, and whole sequences are compared.
 
-Random-init weights (Whisper's init_std 0.02) make the first token's margin over the
-runner-up large, so sequences are long runs of a few tokens; a divergence can only come
-from a near-tie.  Every mismatch is reported with the HF margin at its first divergent
-position."""
+With random-init weights (Whisper's init_std 0.02) greedy sequences are long runs of a
+few tokens.  In fp16 their top-1/top-2 logit margins are wide compared with fp16 spacing,
+and sequences must be identical on >= 99 % of requests.  In bf16 the large-v3 logits
+often tie to within one bf16 step (see the test's docstring), which no two
+implementations with different summation orders resolve alike; there the test checks that
+divergences happen only at such ties."""
+import math
+
 import pytest
 import torch
 
@@ -41,23 +45,41 @@ def _engine(model, dtype):
                                      graph_direct_encoder_kv=True), dec
 
 
-def _margin_at(model, mel, prompt, prefix):
-    """HF top-1 minus top-2 logit (and the top two ids) after prompt + prefix."""
+def _hf_margins(model, mels, prompt, seqs, batch=16):
+    """For every request, the HF decoder's top-1 minus top-2 logit and the top-1 logit at
+    each position of ``seqs`` (teacher-forced on the prompt and the sequence so far), in
+    the model's dtype, with the suppress mask applied."""
     hf = model.hf_model
+    out = []
     with torch.no_grad():
-        e = hf.model.encoder(mel[None].to(DEV, model.dtype)).last_hidden_state
-        ids = torch.tensor([list(prompt) + list(prefix)], device=DEV)
-        h = hf.model.decoder(input_ids=ids, encoder_hidden_states=e).last_hidden_state[0, -1]
-        lg = hf.proj_out(h).float()
-        if model.suppress_mask is not None:
-            lg = lg.masked_fill(model.suppress_mask, float("-inf"))
-        top = lg.topk(2)
-    return float(top.values[0] - top.values[1]), top.indices.tolist()
+        for lo in range(0, len(seqs), batch):
+            hi = min(len(seqs), lo + batch)
+            e = hf.model.encoder(mels[lo:hi].to(DEV, model.dtype)).last_hidden_state
+            ids = torch.tensor([list(prompt) + list(s[:-1]) for s in seqs[lo:hi]], device=DEV)
+            h = hf.model.decoder(input_ids=ids, encoder_hidden_states=e).last_hidden_state[:, len(prompt) - 1:]
+            lg = hf.proj_out(h)
+            if model.suppress_mask is not None:
+                lg = lg.masked_fill(model.suppress_mask, float("-inf"))
+            top = lg.float().topk(2, dim=-1).values
+            out.extend(zip((top[..., 0] - top[..., 1]).tolist(), top[..., 0].tolist()))
+    return out
+
+
+def _ulp(x: float, dtype) -> float:
+    """Spacing of ``dtype`` numbers at magnitude |x|."""
+    return float(torch.finfo(dtype).eps) * 2.0 ** math.floor(math.log2(max(abs(x), 1e-30)))
 
 
 @pytest.mark.parametrize("arch,dtype,n_mels", [("whisper-small", torch.float16, 80),
+                                               ("whisper-large-v3", torch.float16, 128),
                                                ("whisper-large-v3", torch.bfloat16, 128)])
 def test_serving_sequences_match_hf_decoder(arch, dtype, n_mels):
+    """fp16: >= 99 % of requests identical to the HF decoder's sequences.  bf16 (config 5's
+    dtype): random-init large-v3 puts its top two logits within a few bf16 steps of each
+    other (logits near 3 are spaced 2^-6 apart), so the HF decoder itself changes tokens
+    with the batch size; there every divergence must fall on such a near-tie (HF top-2
+    margin within 4 bf16 steps), the requests whose HF path has no near-tie must be >= 99 %
+    identical, and HF's own batch-size self-agreement is reported beside ours."""
     model = PretrainedWhisperModel(config=whisper_config(arch), device=DEV, dtype=dtype, seed=0)
     reqs = synthetic_requests(N_REQ, n_mels, seed=2024, out_lo=N_TOK, out_hi=N_TOK)
     sched, dec = _engine(model, dtype)
@@ -66,16 +88,30 @@ def test_serving_sequences_match_hf_decoder(arch, dtype, n_mels):
     assert r["requests"] == N_REQ and r["failed"] == 0
     ours = r["tokens_by_request"]
     assert all(t is not None and len(t) == N_TOK for t in ours)
+    assert dec.allocated_block_count == 0
     mels = torch.stack([q.mel for q in reqs])
     ref = hf_greedy_tokens(model, mels, prompt, N_TOK, batch=32)
     agree = sequence_agreement(ours, ref)
-    report = []
+    print(f"{arch} {dtype}: {agree['identical']}/{agree['requests']} sequences identical to the HF decoder; "
+          f"first divergences {agree['first_divergence']}")
+    if dtype == torch.float16:
+        assert agree["identical_frac"] >= 0.99, agree
+        return
+    ref8 = hf_greedy_tokens(model, mels, prompt, N_TOK, batch=8)
+    self_agree = sequence_agreement(ref8, ref)
+    margins = _hf_margins(model, mels, prompt, ref)
+    per_req = [margins[i * N_TOK:(i + 1) * N_TOK] for i in range(N_REQ)]
+    near = [[m <= 4 * _ulp(top, dtype) for m, top in row] for row in per_req]
+    bad = []
     for i, (a, b) in enumerate(zip(ours, ref)):
         if a != b:
             k = next(j for j, (x, y) in enumerate(zip(a, b)) if x != y)
-            m, top = _margin_at(model, reqs[i].mel, prompt, b[:k])
-            report.append({"request": i, "first_divergence": k, "ours": a[k], "hf": b[k], "hf_margin": round(m, 5),
-                           "hf_top2": top})
-    print(f"{arch} {dtype}: {agree['identical']}/{agree['requests']} sequences identical; mismatches: {report}")
-    assert dec.allocated_block_count == 0
-    assert agree["identical_frac"] >= 0.99, report
+            if not near[i][k]:
+                bad.append({"request": i, "position": k, "ours": a[k], "hf": b[k], "hf_margin": per_req[i][k][0]})
+    clean = [i for i in range(N_REQ) if not any(near[i])]
+    clean_same = sum(ours[i] == ref[i] for i in clean)
+    print(f"HF batch 8 vs HF batch 32: {self_agree['identical']}/{self_agree['requests']} identical; "
+          f"requests with no near-tie on their HF path: {len(clean)}, of them identical: {clean_same}; "
+          f"divergences away from a near-tie: {bad}")
+    assert not bad, bad
+    assert clean_same >= 0.99 * len(clean)
