@@ -175,9 +175,8 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
   StageMeta* meta = reinterpret_cast<StageMeta*>(setup + 2);  // 16-byte aligned
   int* flag = reinterpret_cast<int*>(meta + S);               // [0] abort, [1..3] spare
   int* ctx_s = flag + 4;                                      // [round4(B)] context lengths
-  int* ip = ctx_s + ((B + 3) & ~3);                           // [B + 1] prefix of queued full chunks
-  int* ipp = ip + ((B + 4) & ~3);                             // [B + 1] prefix of queued partial chunks
-  int* tab_s = ipp + ((B + 4) & ~3);                          // [B * MB] block table copy
+  int* ip = ctx_s + ((B + 3) & ~3);                           // [B + 1] queued-chunk prefix
+  int* tab_s = ip + ((B + 4) & ~3);                           // [B * MB] block table copy
   const bool tab_in_smem = p.table_in_smem != 0;
 
   int* next_item = p.work + 0;  // queue counter
@@ -249,13 +248,8 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
   // ---- 2. producer warp --------------------------------------------------------------
   // Work: chunk c of sequence b (blocks [c*kItemUnits, (c+1)*kItemUnits)) is one item.
   // CTA g starts on chunk g / B of sequence g % B, located with direct loads so that its
-  // copies start one round trip after the wait; the other chunks form a queue handed out
-  // by a global counter once the lengths have arrived: first every chunk whose rows are
-  // all valid (sequence-major), then the shorter last chunks, so the final items handed
-  // out are the small ones.  While more than a grid's worth of items is left, the next
-  // item is taken one step ahead (hiding the atomic's latency); near the end it is taken
-  // only once the current item's copies are issued, so no CTA sits on an item it cannot
-  // start yet.
+  // copies start one round trip after the wait; the other chunks form a queue (sequence-
+  // major) handed out by a global counter once the lengths have arrived.
   if (warp == NW) {
     const uint64_t pol = l2_policy_evict_first();
     int s = 0;
@@ -359,10 +353,10 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
       for (int i = lane; i < B; i += 32) ctx_s[i] = p.context_lens[i];
     __syncwarp();
     {
-      int carry = 0, carryp = 0;
+      int carry = 0;
       for (int base = 0; base < B; base += 32) {
         const int i = base + lane;
-        int v = 0, vp = 0;
+        int v = 0;
         if (i < B) {
           const int c0 = ctx_s[i];
           if (c0 > max_ctx) set_error(p.err, SPD_DEVERR_LENGTH);
@@ -370,29 +364,17 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
           ctx_s[i] = c;
           const int nch = ((c + BS - 1) / BS + kItemUnits - 1) / kItemUnits;
           const int started = i < G ? min((G - 1 - i) / B + 1, nch) : 0;
-          // the last chunk is "partial" when it has fewer than kItemUnits * BS rows; it
-          // joins the queue's second phase unless a CTA started on it
-          const int part = (c % (kItemUnits * BS) != 0 && nch - 1 >= started) ? 1 : 0;
-          v = nch - started - part;
-          vp = part;
+          v = nch - started;
         }
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const int n = __shfl_up_sync(0xffffffffu, v, o);
-          const int np = __shfl_up_sync(0xffffffffu, vp, o);
-          if (lane >= o) {
-            v += n;
-            vp += np;
-          }
+          if (lane >= o) v += n;
         }
-        if (i < B) {
-          ip[i + 1] = v + carry;
-          ipp[i + 1] = vp + carryp;
-        }
+        if (i < B) ip[i + 1] = v + carry;
         carry += __shfl_sync(0xffffffffu, v, 31);
-        carryp += __shfl_sync(0xffffffffu, vp, 31);
       }
-      if (lane == 0) ip[0] = ipp[0] = 0;
+      if (lane == 0) ip[0] = 0;
     }
     __syncwarp();
     if (lane == 0) SPD_TRACE(1);
@@ -401,30 +383,21 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
       if (ctx_s[b] == 0)
         for (int i = lane; i < HD; i += 32) out[(size_t)b * HD + i] = Elem<T>::from_f(0.f);
     if (lane == 0) {
-      const int n_full = ip[B];
-      const int n_queue = n_full + ipp[B];
+      const int n_queue = ip[B];
       alive = alive && !flag[0];
       while (alive && q < n_queue) {
-        const bool ahead = n_queue - q > G;
-        int nxt = ahead ? atomicAdd(next_item, 1) : 0;  // next take, in flight meanwhile
-        int b, c;
-        const bool full_phase = q < n_full;
-        b = full_phase ? upper_index_i32(ip, B, q) : upper_index_i32(ipp, B, q - n_full);
+        const int nxt = atomicAdd(next_item, 1);  // next take, in flight meanwhile
+        const int b = upper_index_i32(ip, B, q);
         const int ctx = ctx_s[b];
         const int nblk = (ctx + BS - 1) / BS;
         const int nch = (nblk + kItemUnits - 1) / kItemUnits;
-        if (full_phase) {
-          const int started = b < G ? min((G - 1 - b) / B + 1, nch) : 0;
-          c = started + (q - ip[b]);
-        } else {
-          c = nch - 1;
-        }
+        const int started = b < G ? min((G - 1 - b) / B + 1, nch) : 0;
+        const int c = started + (q - ip[b]);
         const int j0 = c * kItemUnits, j1 = min(j0 + kItemUnits, nblk);
         for (int j = j0; j < j1 && alive; ++j) {
           const int phys = tab_in_smem ? tab_s[b * MB + j] : p.block_tables[(size_t)b * MB + j];
           issue_unit(b, j, ctx, phys, c, nch, j == j0, j == j1 - 1);
         }
-        if (!ahead) nxt = atomicAdd(next_item, 1);
         q = nxt;
       }
       SPD_TRACE(3);
@@ -733,27 +706,21 @@ __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
   const size_t stride = (size_t)p.H * kPartialRow<D>;  // next item, same head
   T* orow = reinterpret_cast<T*>(p.out) + ((size_t)b * p.H + h) * D;
   if (nitems <= MAXI) {
-    // Every lane loads every item's (m, l) (the same addresses across the warp) and its own
-    // EPL elements of every item's acc, all in one round of loads; the weights are then
-    // computed lane-locally, without shuffles.
-    float2 ml[MAXI];
-    V a[MAXI];
+    // lane l holds elements [l*EPL, (l+1)*EPL) of every item's acc: one vector load per item
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (lane < nitems) ml = __ldcg(reinterpret_cast<const float2*>(base + lane * stride + D));
     const bool hold = lane < D / EPL;
+    V a[MAXI];
 #pragma unroll
-    for (int it = 0; it < MAXI; ++it) {
-      ml[it] = it < nitems ? __ldcg(reinterpret_cast<const float2*>(base + it * stride + D))
-                           : make_float2(-INFINITY, 0.f);
+    for (int it = 0; it < MAXI; ++it)
       a[it] = (it < nitems && hold) ? __ldcg(reinterpret_cast<const V*>(base + it * stride) + lane) : V{};
-    }
-    float M = ml[0].x;
-#pragma unroll
-    for (int it = 1; it < MAXI; ++it) M = fmaxf(M, ml[it].x);
-    float L = 0.f;
+    const float M = warp_max(ml.x);
+    const float w = lane < nitems ? exp2f(ml.x - M) : 0.f;
+    const float inv = 1.f / warp_sum(ml.y * w);
     V o{};
 #pragma unroll
     for (int it = 0; it < MAXI; ++it) {
-      const float wi = ex2_approx(ml[it].x - M);  // 0 for the unused items (m = -inf)
-      L = fmaf(wi, ml[it].y, L);
+      const float wi = __shfl_sync(0xffffffffu, w, it);
       o.x = fmaf(wi, a[it].x, o.x);
       o.y = fmaf(wi, a[it].y, o.y);
       if constexpr (EPL == 4) {
@@ -761,7 +728,6 @@ __global__ void __launch_bounds__(128) paged_merge_kernel(const PagedParams p) {
         o.w = fmaf(wi, a[it].w, o.w);
       }
     }
-    const float inv = 1.f / L;
     if (hold) {
       T* dst = orow + lane * EPL;
       dst[0] = Elem<T>::from_f(o.x * inv);
@@ -821,7 +787,7 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
                      (reinterpret_cast<uintptr_t>(p.block_tables) & 15) == 0)
                         ? 1
                         : 0;
-  const size_t fixed = 16 * 8 /*barriers*/ + 32 * 8 /*meta*/ + 16 + 4 * ((size_t)p.B + 4) * 3 +
+  const size_t fixed = 16 * 8 /*barriers*/ + 32 * 8 /*meta*/ + 16 + 4 * ((size_t)p.B + 4) * 2 +
                        (p.table_in_smem ? tab_bytes : 0) + 256;
   // Ring depth: up to ~216 KB per CTA (one CTA per SM at the Whisper shapes; the
   // producer warp keeps every stage in flight), at least two stages.
@@ -831,7 +797,7 @@ static int launch_paged(const PagedParams& base, int device_sms, cudaStream_t st
   S = S < 1 ? 1 : (S > 8 ? 8 : S);
   p.stages = S;
   const size_t smem = round_up((size_t)S * stage_bytes, 128) + 16 * ((size_t)S * 2 + 2) + 32 * (size_t)S + 16 +
-                      4 * ((((size_t)p.B + 3) & ~(size_t)3) + 2 * (((size_t)p.B + 4) & ~(size_t)3)) +
+                      4 * ((((size_t)p.B + 3) & ~(size_t)3) + (((size_t)p.B + 4) & ~(size_t)3)) +
                       (p.table_in_smem ? tab_bytes : 0);
   if (smem > (PAIR ? 113 : 227) * 1024) return SPD_ERR_UNSUPPORTED;
   auto kfn = paged_decode_attn_kernel<T, D, BS, HPW, PAIR>;

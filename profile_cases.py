@@ -15,8 +15,11 @@ Cases:
   proj_small    the handoff cross-KV projection of one 1500-position request, Whisper-small
   proj_large    the same for Whisper-large-v3
   decode_small  one decode step of random-init Whisper-small (fp16) over 64 graph slots
-                with 800-position cross contexts and 100-token self contexts, replayed
+                with the full 1500-position cross contexts (what serving attends) and
+                100-token self contexts, replayed
                 from its CUDA graph; launches run inside an NVTX range named "steps"
+  decode_large  the same for random-init Whisper-large-v3 (bf16) with the full
+                1500-position cross contexts the serving configuration attends
 
 Each launch reads a different input set (``--sets``) so that DRAM counters see cold data.
 ``--trace`` loads the trace build of the library (inference-speech-model_b200/csrc/build.py
@@ -99,18 +102,19 @@ def _proj(torch, ops, dev, sets, d, L, H, name):
     return lambda i: ops.cross_kv_project(enc[i % sets], w, b, out)
 
 
-def _decode_small(torch, ops, dev, sets, B=64, cross_len=800, self_len=100):
-    """One batch-64 decode step of random-init Whisper-small (fp16) replayed from its graph."""
+def _decode_small(torch, ops, dev, sets, B=64, cross_len=1500, self_len=100, arch="whisper-small",
+                  dtype_name="float16", name="decode_small"):
+    """One batch-64 decode step of a random-init Whisper model replayed from its graph."""
     from speech_serving.block_manager import BlockManager
     from speech_serving.graph_decode_buffers import PagedDecodeState
     from speech_serving.models import PretrainedWhisperModel
     from speech_serving.serving import whisper_config
 
-    model = PretrainedWhisperModel(config=whisper_config("whisper-small"), device=str(dev), dtype=torch.float16,
-                                   seed=0)
+    dt = getattr(torch, dtype_name)
+    model = PretrainedWhisperModel(config=whisper_config(arch), device=str(dev), dtype=dt, seed=0)
     L, H, D = model.num_decoder_layers, model.num_heads, model.head_dim
     nblk = -(-(self_len + 8) // 16)
-    bm = BlockManager(L, H, D, 16, B * nblk + 8, dtype=torch.float16, device=str(dev))
+    bm = BlockManager(L, H, D, 16, B * nblk + 8, dtype=dt, device=str(dev))
     st = PagedDecodeState(model, bm, B, max_blocks=nblk, device=str(dev))
     g = torch.Generator(device=dev).manual_seed(1)
     st.cross_kv.normal_(generator=g)
@@ -134,7 +138,7 @@ def _decode_small(torch, ops, dev, sets, B=64, cross_len=800, self_len=100):
     w_bytes = sum(p.numel() * p.element_size() for n, p in model.hf_model.model.decoder.named_parameters()
                   if "embed_" not in n) + model.hf_model.proj_out.weight.numel() * 2
     kv_bytes = L * B * 2 * H * D * 2 * (cross_len + self_len)
-    WORK["decode_small"] = (w_bytes + kv_bytes, "GB/s", None)
+    WORK[name] = (w_bytes + kv_bytes, "GB/s", None)
 
     def run(i):
         st.ctx_lens.copy_(ctx0)  # every replay attends the same self_len positions
@@ -151,6 +155,8 @@ CASES = {
     "proj_small": lambda t, o, dev, n: _proj(t, o, dev, n, 768, 12, 12, "proj_small"),
     "proj_large": lambda t, o, dev, n: _proj(t, o, dev, n, 1280, 32, 20, "proj_large"),
     "decode_small": lambda t, o, dev, n: _decode_small(t, o, dev, n),
+    "decode_large": lambda t, o, dev, n: _decode_small(t, o, dev, n, cross_len=1500, arch="whisper-large-v3",
+                                                       dtype_name="bfloat16", name="decode_large"),
 }
 
 POINTS = {0: ["entry", "first lengths scanned", "first copy issued", "producer out of items", "first stage consumed",
