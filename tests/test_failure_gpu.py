@@ -5,7 +5,7 @@ SPD_DEVERR_TIMEOUT in the launch's error word, the launch abandons its work, wai
 the default bound) for its own copies still in flight and returns, so the context stays
 usable.  The first test makes a wait run out on purpose: a barrier phase that nothing
 completes, under a 1 ms bound.  The others give real launches a 1 ns bound: a wait
-then gives up as soon as one suspended try on its barrier comes back empty (whether the
+then gives up once 64 suspended tries on its barrier have come back empty (whether the
 data beats that depends on the hardware's suspend interval), so each such launch either
 completes exactly or stops with SPD_DEVERR_TIMEOUT — never faults — and the next launches
 on the same context and workspace, under the default bound, are exact.  Nothing here
