@@ -50,7 +50,8 @@
 // Timeline marks (trace builds only; see spd_trace.cuh).  Streaming kernel, per CTA:
 // 0 entry, 6 griddepcontrol.wait returned, 2 first copy issued, 1 lengths scanned,
 // 3 producer out of items, 4 first stage consumed (warp 0), 5 warp 0 done, 7 producer
-// done.  Merge kernel, per CTA: 0 entry, 1 griddepcontrol.wait returned, 2 done.
+// done, 8 last stage landed (seen by warp 0), 9 stages warp 0 processed (a count).
+// Merge kernel, per CTA: 0 entry, 1 griddepcontrol.wait returned, 2 done.
 SPD_TRACE_ARRAY
 #define SPD_TRACE(point) SPD_TRACE_AT(0, point)
 #define SPD_TRACE_MERGE(point) SPD_TRACE_AT(1, point)
@@ -447,6 +448,7 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
   int s = 0;
   uint32_t ph = 0;
   bool traced = false;
+  int n_stages = 0;
   for (;;) {
     if (*((volatile int*)&flag[0]) || !mbar_wait_bounded(&full[s], ph, p.err, p.wait_ns)) {
       flag[0] = 1;
@@ -454,9 +456,11 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
     }
     const StageMeta mt = meta[s];
     if (mt.b < 0) break;
-    if (tid == 0 && !traced) {
-      SPD_TRACE(4);
+    if (tid == 0) {
+      if (!traced) SPD_TRACE(4);
       traced = true;
+      SPD_TRACE(8);
+      ++n_stages;
     }
     const int b = mt.b;
     const int nvalid = mt.nvalid;
@@ -671,7 +675,11 @@ __global__ void __launch_bounds__(PAIR ? kPairThreads : 544, PAIR ? 2 : 1)
       }
     }
   }
-  if (tid == 0) SPD_TRACE(5);
+  if (tid == 0) {
+    SPD_TRACE(5);
+    SPD_TRACE_VALUE(0, 9, n_stages);
+  }
+  (void)n_stages;
 }
 
 // ------------------------------------------------------------------ merge kernel

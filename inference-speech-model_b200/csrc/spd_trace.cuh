@@ -12,7 +12,7 @@
 
 namespace spd {
 constexpr int kTraceCtas = 1024;  // CTAs recorded per kernel (blockIdx.x modulo this)
-constexpr int kTracePoints = 8;   // marks per CTA
+constexpr int kTracePoints = 12;  // marks per CTA
 constexpr int kTraceKernels = 2;  // streaming kernel, merge kernel
 }  // namespace spd
 
@@ -21,10 +21,12 @@ constexpr int kTraceKernels = 2;  // streaming kernel, merge kernel
   namespace spd {                                                                                \
   static __device__ unsigned long long g_trace[kTraceKernels * kTraceCtas * kTracePoints];       \
   }
-#define SPD_TRACE_AT(kernel, point)                                                              \
+#define SPD_TRACE_AT(kernel, point) SPD_TRACE_VALUE(kernel, point, spd::global_ns())
+#define SPD_TRACE_VALUE(kernel, point, value)                                                    \
   (spd::g_trace[((kernel) * spd::kTraceCtas + (blockIdx.x % spd::kTraceCtas)) * spd::kTracePoints + \
-                (point)] = spd::global_ns())
+                (point)] = (unsigned long long)(value))
 #else
 #define SPD_TRACE_ARRAY
 #define SPD_TRACE_AT(kernel, point) ((void)0)
+#define SPD_TRACE_VALUE(kernel, point, value) ((void)0)
 #endif

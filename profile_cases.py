@@ -160,7 +160,7 @@ CASES = {
 }
 
 POINTS = {0: ["entry", "first lengths scanned", "first copy issued", "producer out of items", "first stage consumed",
-              "warp 0 done", "griddepcontrol.wait returned", "producer done"],
+              "warp 0 done", "griddepcontrol.wait returned", "producer done", "last stage landed"],
           1: ["entry", "griddepcontrol.wait returned", "done"]}
 
 
@@ -169,7 +169,7 @@ def _fetch_trace(lib):
 
     import numpy as np
 
-    kernels, ctas, points = 2, 1024, 8
+    kernels, ctas, points = 2, 1024, 12
     buf = (C.c_ulonglong * (kernels * ctas * points))()
     fn = lib.spd_trace_fetch_paged
     fn.restype = C.c_int
@@ -180,7 +180,8 @@ def _fetch_trace(lib):
 
 
 def _summarise_trace(tr):
-    """Per mark: when the CTAs reached it (µs after the first CTA's entry): min, median, max."""
+    """Per mark: when the CTAs reached it (µs after the first CTA's entry): min, median, max;
+    then, per CTA of the streaming kernel, its stage count against its finishing time."""
     t0 = tr[0][:, 0][tr[0][:, 0] > 0].min()
     print("mark (µs after the first CTA entered)           CTAs    min   median      max")
     for k, names in POINTS.items():
@@ -193,6 +194,16 @@ def _summarise_trace(tr):
             kname = "stream" if k == 0 else "merge "
             print(f"{kname} {pt} {name:<38s} {v.size:5d} {us.min():7.2f} {float(sorted(us)[len(us) // 2]):8.2f} "
                   f"{us.max():8.2f}")
+    live = tr[0][:, 0] > 0
+    stages = tr[0][live, 9]
+    done = (tr[0][live, 5] - t0) / 1e3
+    landed = (tr[0][live, 8] - t0) / 1e3
+    order = done.argsort()
+    print("stages per CTA (warp 0): min %d median %d max %d" % (stages.min(), sorted(stages)[len(stages) // 2],
+                                                               stages.max()))
+    print("CTAs by finishing time: (done µs, last landed µs, stages) of the first, median and last five")
+    for i in list(order[:5]) + list(order[len(order) // 2:len(order) // 2 + 5]) + list(order[-5:]):
+        print(f"  {done[i]:6.2f} {landed[i]:6.2f} {int(stages[i]):3d}")
 
 
 def main():
