@@ -39,6 +39,10 @@
  *   spd_argmax_rows        the greedy pick after the output projection:
  *                          speech_serving/graph_decode_buffers.py:446-448 (suppress mask,
  *                          argmax) and speech_serving/models.py:487
+ *   spd_linear             the decode step's Linear layers: speech_serving/models.py:127-129
+ *                          (q/k/v), :159 (self out), :178-180 (cross q), :202 (cross out),
+ *                          :205-207 (MLP with GELU), :487 (lm_head), and the same layers of
+ *                          transformers' WhisperDecoderLayer / proj_out (models.py:593-603)
  */
 #ifndef SPD_B200_H
 #define SPD_B200_H
@@ -194,6 +198,24 @@ int spd_add_layernorm(const void* x, const void* delta, const void* gamma, const
  * out is int64 [rows]; ld >= cols (elements between rows). */
 int spd_argmax_rows(const void* x, int rows, int cols, int64_t ld, const void* skip_mask, int64_t* out,
                     int dtype, void* stream);
+
+/* Small-batch Linear layer (the decode step's projections, MLP and head) on the tensor
+ * cores (tcgen05, weights streamed by TMA, K split over a thread-block cluster when N is
+ * small):
+ *   y(m, n) = act( sum_k x[m*K + k] * w[n*K + k] + bias[n] )   m < M, n < N
+ * x [M][K] and w [N][K] row-major (w is an nn.Linear weight), bias [N] or NULL,
+ * activation SPD_ACT_NONE or SPD_ACT_GELU (the erf form, as torch's default GELU).
+ * Output column n is written to plane n / y_group_cols, planes y_group_stride elements
+ * apart, each [M][y_group_cols] (y_group_cols = N: a plain [M][N] output; a packed q|k|v
+ * weight with y_group_cols = H*D writes q, k and v as three [M][H*D] tensors).
+ * fp32 accumulation, one rounding to dtype.  Requires dtype F16 or BF16, 1 <= M <= 64,
+ * K a multiple of 64, N a multiple of y_group_cols, x and w 16-byte aligned.
+ * error_word: optional int32 device word receiving SPD_DEVERR_TIMEOUT. */
+#define SPD_ACT_NONE 0
+#define SPD_ACT_GELU 1
+int spd_linear(const void* x, const void* w, const void* bias, void* y, int M, int N, int K,
+               int64_t y_group_cols, int64_t y_group_stride, int activation, int dtype,
+               int32_t* error_word, void* stream);
 
 /* Allocation-free variant of spd_paged_decode_attn, for callers that cannot allocate
  * GPU memory or own a workspace: code running where cudaMalloc is unavailable or

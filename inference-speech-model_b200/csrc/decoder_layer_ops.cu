@@ -10,17 +10,44 @@
 // The statistics are taken from the rounded x_out, as when the add and the LayerNorm
 // run one after the other in the model dtype, and accumulate in fp32 (two passes over
 // the row held in registers).  x_out may alias x.
+//
+// Both kernels here are launched with programmatic dependent launch: they signal
+// launch_dependents on entry, so a PDL-launched kernel behind them (the small-batch GEMM
+// that consumes the LayerNorm output) gets resident and prefetches its weights while
+// they run, and they wait (griddepcontrol.wait) for the kernel before them only when
+// they first read an input it may have written; gamma and beta are parameters, read
+// before that wait.
 #include "spd_params.cuh"
 
 namespace spd {
+
+// Launches kfn(args) on `st` with programmatic stream serialization allowed.
+template <typename K, typename... Args>
+static int launch_pdl(K kfn, dim3 grid, dim3 block, cudaStream_t st, const Args&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kfn, args...) == cudaSuccess ? SPD_OK : SPD_ERR_CUDA;
+}
 
 // VPL: 16-byte vectors per lane (a row of up to 32 * VPL vectors).
 template <typename T, int VPL>
 __global__ void __launch_bounds__(128) add_layernorm_kernel(const AddLnParams p) {
   constexpr int E = 16 / sizeof(T);  // elements per vector
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  if (row >= p.rows) return;
+  if (row >= p.rows) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    return;
+  }
   const int nvec = p.cols / E;
   const T* x = reinterpret_cast<const T*>(p.x) + row * p.cols;
   const T* dl = p.delta ? reinterpret_cast<const T*>(p.delta) + row * p.cols : nullptr;
@@ -38,6 +65,7 @@ __global__ void __launch_bounds__(128) add_layernorm_kernel(const AddLnParams p)
       }
     }
   }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // x and delta may come from the previous kernel
   float v[VPL][E];
   float sum = 0.f;
 #pragma unroll
@@ -107,27 +135,21 @@ static int add_ln_dispatch(const AddLnParams& p, cudaStream_t st) {
   const int vpl = (nvec + 31) / 32;
   // four rows per CTA: a decode step's few rows spread over more SMs
   const unsigned grid = (unsigned)((p.rows + 3) / 4);
+  auto run = [&](auto kfn) { return launch_pdl(kfn, dim3(grid), dim3(128), st, p); };
   switch (vpl) {
-    case 1: add_layernorm_kernel<T, 1><<<grid, 128, 0, st>>>(p); break;
-    case 2: add_layernorm_kernel<T, 2><<<grid, 128, 0, st>>>(p); break;
-    case 3: add_layernorm_kernel<T, 3><<<grid, 128, 0, st>>>(p); break;
-    case 4: add_layernorm_kernel<T, 4><<<grid, 128, 0, st>>>(p); break;
-    case 5: case 6: add_layernorm_kernel<T, 6><<<grid, 128, 0, st>>>(p); break;
-    case 7: case 8: add_layernorm_kernel<T, 8><<<grid, 128, 0, st>>>(p); break;
+    case 1: return run(add_layernorm_kernel<T, 1>);
+    case 2: return run(add_layernorm_kernel<T, 2>);
+    case 3: return run(add_layernorm_kernel<T, 3>);
+    case 4: return run(add_layernorm_kernel<T, 4>);
+    case 5: case 6: return run(add_layernorm_kernel<T, 6>);
+    case 7: case 8: return run(add_layernorm_kernel<T, 8>);
     default:
       if constexpr (sizeof(T) == 4) {  // fp32 rows of up to 2048 elements
-        if (vpl <= 12) {
-          add_layernorm_kernel<T, 12><<<grid, 128, 0, st>>>(p);
-          break;
-        }
-        if (vpl <= 16) {
-          add_layernorm_kernel<T, 16><<<grid, 128, 0, st>>>(p);
-          break;
-        }
+        if (vpl <= 12) return run(add_layernorm_kernel<T, 12>);
+        if (vpl <= 16) return run(add_layernorm_kernel<T, 16>);
       }
       return SPD_ERR_UNSUPPORTED;
   }
-  return cudaPeekAtLastError() == cudaSuccess ? SPD_OK : SPD_ERR_CUDA;
 }
 
 // ------------------------------------------------------------------ greedy token pick
@@ -151,6 +173,8 @@ __device__ __forceinline__ bool arg_better(float av, int ai, float bv, int bi) {
 template <typename T>
 __global__ void __launch_bounds__(1024) argmax_rows_kernel(const ArgmaxParams p) {
   constexpr int E = 16 / sizeof(T);
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the logits come from the previous kernel
   const T* x = reinterpret_cast<const T*>(p.x) + (long long)blockIdx.x * p.ld;
   const unsigned char* skip = reinterpret_cast<const unsigned char*>(p.skip);
   ArgBest best{-INFINITY, 0x7fffffff};
@@ -209,12 +233,11 @@ __global__ void __launch_bounds__(1024) argmax_rows_kernel(const ArgmaxParams p)
 int argmax_rows_launch(const ArgmaxParams& p, int dtype, cudaStream_t st) {
   const unsigned threads = p.cols >= 8192 ? 1024u : 256u;
   switch (dtype) {
-    case SPD_F32: argmax_rows_kernel<float><<<p.rows, threads, 0, st>>>(p); break;
-    case SPD_F16: argmax_rows_kernel<__half><<<p.rows, threads, 0, st>>>(p); break;
-    case SPD_BF16: argmax_rows_kernel<__nv_bfloat16><<<p.rows, threads, 0, st>>>(p); break;
+    case SPD_F32: return launch_pdl(argmax_rows_kernel<float>, dim3(p.rows), dim3(threads), st, p);
+    case SPD_F16: return launch_pdl(argmax_rows_kernel<__half>, dim3(p.rows), dim3(threads), st, p);
+    case SPD_BF16: return launch_pdl(argmax_rows_kernel<__nv_bfloat16>, dim3(p.rows), dim3(threads), st, p);
     default: return SPD_ERR_UNSUPPORTED;
   }
-  return cudaPeekAtLastError() == cudaSuccess ? SPD_OK : SPD_ERR_CUDA;
 }
 
 int add_layernorm_launch(const AddLnParams& p, int dtype, cudaStream_t st) {

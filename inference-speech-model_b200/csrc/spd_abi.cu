@@ -18,6 +18,9 @@ int kv_append_launch(const AppendParams& p, int sms, cudaStream_t st);
 int block_gather_launch(const GatherParams& p, int sms, cudaStream_t st);
 int add_layernorm_launch(const AddLnParams& p, int dtype, cudaStream_t st);
 int argmax_rows_launch(const ArgmaxParams& p, int dtype, cudaStream_t st);
+int linear_small_m_launch(const void* x, const void* w, const void* bias, void* y, int M, int N, int K,
+                          long long group_cols, long long group_stride, int act, int dtype, int* err, int sms,
+                          cudaStream_t st);
 int cross_kv_project_launch(const void* enc_out, const void* w_kv, const void* b_kv, void* out,
                             const int32_t* slot_ids, int B, int T, int d_model, int L, int H, int D,
                             int T_out, int64_t out_slot_stride, int dtype, int* err, int sms, cudaStream_t st);
@@ -331,6 +334,30 @@ int spd_argmax_rows(const void* x, int rows, int cols, int64_t ld, const void* s
                       (aligned16(x) && (ld * eb) % 16 == 0) ? 1 : 0};
   const int rc = spd::argmax_rows_launch(p, dtype, static_cast<cudaStream_t>(stream));
   if (rc != SPD_OK) return fail(rc, "spd_argmax_rows: launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  return ok();
+}
+
+int spd_linear(const void* x, const void* w, const void* bias, void* y, int M, int N, int K, int64_t y_group_cols,
+               int64_t y_group_stride, int activation, int dtype, int32_t* error_word, void* stream) {
+  if (dtype != SPD_F16 && dtype != SPD_BF16)
+    return fail(SPD_ERR_UNSUPPORTED, "spd_linear: dtype %d not supported (F16/BF16 only)", dtype);
+  if (!x || !w || !y) return fail(SPD_ERR_INVALID_ARG, "spd_linear: null pointer");
+  if (M < 1 || M > 64 || N < 1 || K < 64 || K % 64)
+    return fail(SPD_ERR_UNSUPPORTED, "spd_linear: need 1 <= M <= 64 and K a multiple of 64 (M=%d N=%d K=%d)", M, N,
+                K);
+  if (y_group_cols <= 0) y_group_cols = N;
+  if (N % y_group_cols || (N > y_group_cols && y_group_stride < (int64_t)M * y_group_cols))
+    return fail(SPD_ERR_INVALID_ARG, "spd_linear: N must be a multiple of y_group_cols, planes must not overlap");
+  if (activation != SPD_ACT_NONE && activation != SPD_ACT_GELU)
+    return fail(SPD_ERR_INVALID_ARG, "spd_linear: unknown activation %d", activation);
+  if (!aligned16(x) || !aligned16(w) || (reinterpret_cast<uintptr_t>(y) & 1) ||
+      (bias && (reinterpret_cast<uintptr_t>(bias) & 1)))
+    return fail(SPD_ERR_INVALID_ARG, "spd_linear: x and w must be 16-byte aligned");
+  const int sms = sm_count(-1);
+  if (sms <= 0) return fail(SPD_ERR_CUDA, "spd_linear: no CUDA device");
+  const int rc = spd::linear_small_m_launch(x, w, bias, y, M, N, K, y_group_cols, y_group_stride, activation, dtype,
+                                            error_word, sms, static_cast<cudaStream_t>(stream));
+  if (rc != SPD_OK) return fail(rc, "spd_linear: launch failed: %s", cudaGetErrorString(cudaGetLastError()));
   return ok();
 }
 

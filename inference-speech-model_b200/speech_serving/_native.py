@@ -29,6 +29,8 @@ SPD_DEVERR_BLOCK_ID = 1
 SPD_DEVERR_LENGTH = 2
 SPD_DEVERR_TIMEOUT = 4
 
+SPD_ACT_NONE, SPD_ACT_GELU = 0, 1
+
 # Every symbol the header declares, with (restype, argtypes).
 _vp, _i, _i64, _f, _sz = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
 _SIGNATURES = {
@@ -46,6 +48,7 @@ _SIGNATURES = {
     "spd_cross_kv_project": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _i, _vp, _vp]),
     "spd_add_layernorm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i64, _f, _i, _vp]),
     "spd_argmax_rows": (_i, [_vp, _i, _i, _i64, _vp, _vp, _i, _vp]),
+    "spd_linear": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i64, _i64, _i, _i, _vp, _vp]),
     "spd_set_wait_timeout_ns": (_i, [C.c_uint64]),
     "spd_get_wait_timeout_ns": (C.c_uint64, []),
     "spd_selftest_wait_timeout": (_i, [_vp, C.c_uint64, _vp]),

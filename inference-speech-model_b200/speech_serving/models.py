@@ -115,6 +115,32 @@ def _padded_head(model: nn.Module, linear: nn.Linear, multiple: int = 64) -> tor
     return wp
 
 
+def _tc_linear_ok(x: torch.Tensor, K: int) -> bool:
+    """True when ``ops.linear`` (the small-batch tcgen05 GEMM) takes this input: 16-bit,
+    at most 64 rows, K a multiple of 64.  The decode steps use it for the MLP: fc1 with
+    its GELU fused (one launch instead of a GEMM and an elementwise kernel) and fc2, which
+    measured at least even with cuBLAS at batch 64.  The q/k/v and d x d projections and
+    the vocabulary-padded head stay on cuBLAS, which measured faster for those shapes
+    (profile_cases.py linear_table, and the decode_small / decode_large steps)."""
+    return x.dtype in (torch.float16, torch.bfloat16) and x.shape[0] <= 64 and K % 64 == 0
+
+
+def _mlp(h: torch.Tensor, fc1: nn.Linear, fc2: nn.Linear, act_is_gelu: bool, act) -> torch.Tensor:
+    """fc2(act(fc1(h))), with fc1 + GELU and fc2 on the tcgen05 kernel when it applies."""
+    if act_is_gelu and _tc_linear_ok(h, fc1.in_features) and fc2.in_features % 64 == 0:
+        u = ops.linear(h.contiguous(), fc1.weight, fc1.bias, gelu=True)
+        return ops.linear(u, fc2.weight, fc2.bias)
+    return fc2(act(fc1(h)))
+
+
+def _head_logits(model: nn.Module, h: torch.Tensor, head: nn.Linear) -> torch.Tensor:
+    """[n, >= vocab] logits of the output projection: cuBLAS on the vocabulary-padded
+    weight (an unpadded vocabulary makes cuBLAS pick a slow kernel)."""
+    if head.bias is not None:
+        return F.linear(h, head.weight, head.bias)
+    return F.linear(h, _padded_head(model, head))
+
+
 class _LayerKV:
     """Keys/values of one decoder layer ([B, H, T, D]), named like a DynamicCache layer."""
 
@@ -306,8 +332,10 @@ class WhisperClassSpeechEncoderDecoderModel(nn.Module):
                                     workspace=st.cross_ws[n])
             x, h = ops.add_layernorm(x, layer.cross_attn_out(c.view(n, -1)), layer.norm3)
             nxt = layers[l + 1].norm1 if l + 1 < len(layers) else self.decoder_norm
-            x, h = ops.add_layernorm(x, layer.mlp(h), nxt)
-        return ops.argmax_rows(F.linear(h, _padded_head(self, self.lm_head)), self.vocab_size)
+            mlp = _mlp(h, layer.mlp[0], layer.mlp[2], isinstance(layer.mlp[1], nn.GELU) and
+                       layer.mlp[1].approximate == "none", layer.mlp[1])
+            x, h = ops.add_layernorm(x, mlp, nxt)
+        return ops.argmax_rows(_head_logits(self, h, self.lm_head), self.vocab_size)
 
 
 class PretrainedWhisperModel(nn.Module):
@@ -533,11 +561,10 @@ class PretrainedWhisperModel(nn.Module):
             c = ops.cross_attention(cq, st.cross_kv[:n, l, 0], st.cross_kv[:n, l, 1], st.cross_lens[:n], scale=1.0,
                                     workspace=st.cross_ws[n])
             x, h = ops.add_layernorm(x, ea.out_proj(c.view(n, -1)), layer.final_layer_norm)
-            mlp = layer.fc2(layer.activation_fn(layer.fc1(h)))
+            mlp = _mlp(h, layer.fc1, layer.fc2, self.config.activation_function == "gelu", layer.activation_fn)
             if l + 1 < len(layers):
                 x, _ = ops.add_layernorm(x, mlp, layers[l + 1].self_attn_layer_norm, out_y=qkv_in[:, :d])
             else:
                 x, h = ops.add_layernorm(x, mlp, dec.layer_norm)
         # the suppress mask and the argmax over the vocabulary in one kernel
-        return ops.argmax_rows(F.linear(h, _padded_head(self, self.hf_model.proj_out)), self.vocab_size,
-                               self.suppress_mask)
+        return ops.argmax_rows(_head_logits(self, h, self.hf_model.proj_out), self.vocab_size, self.suppress_mask)

@@ -15,6 +15,8 @@ Ops and the reference code they replace:
   block_gather            speech_serving/phase_aware_scheduler.py:613-624, :859-882;
                           speech_serving/encoder_attention.py:50-63
   cross_kv_project        speech_serving/models.py:554-561
+  linear                  the decode step's Linear layers (speech_serving/models.py:127-129,
+                          :159, :178-180, :202, :205-207, :487)
 """
 from __future__ import annotations
 
@@ -326,6 +328,39 @@ def cross_kv_project(
         enc_out.data_ptr(), w_kv.data_ptr(), _ptr(b_kv), out.data_ptr(), _ptr(slot_ids), B, T, d, L, H, D, T_out,
         out.stride(0), dtype_code(enc_out.dtype), _ptr(error_word), _stream_handle())
     N.check(rc, "spd_cross_kv_project")
+    return out
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, gelu: bool = False,
+           out: Optional[torch.Tensor] = None, groups: int = 1,
+           error_word: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``act(x @ weight.T + bias)`` for a small batch (x [M, K], M <= 64, K a multiple
+    of 64; weight [N, K] as nn.Linear keeps it; 16-bit dtypes) on the tensor cores, GELU
+    (erf form) fused when ``gelu``.  With ``groups`` > 1 the N output columns are split into
+    that many equal groups written as separate [M, N / groups] tensors, stacked:
+    out [groups, M, N / groups] (a packed q|k|v weight gives q, k and v)."""
+    _require_cuda("linear", x, weight, bias, out, error_word)
+    if x.dim() != 2 or weight.dim() != 2 or not x.is_contiguous() or not weight.is_contiguous():
+        raise RuntimeError("linear: x [M, K] and weight [N, K] must be contiguous 2-D tensors")
+    M, K = x.shape
+    Nf = weight.shape[0]
+    if weight.shape[1] != K or Nf % groups:
+        raise RuntimeError(f"linear: weight {tuple(weight.shape)} does not match x {tuple(x.shape)} / groups={groups}")
+    for t in (weight, bias, out):
+        if t is not None and t.dtype != x.dtype:
+            raise RuntimeError("linear: all tensors must share x's dtype")
+    if bias is not None and (bias.shape != (Nf,) or not bias.is_contiguous()):
+        raise RuntimeError("linear: bias must be a contiguous [N] tensor")
+    gc = Nf // groups
+    shape = (groups, M, gc) if groups > 1 else (M, Nf)
+    if out is None:
+        out = torch.empty(shape, dtype=x.dtype, device=x.device)
+    elif tuple(out.shape) != shape or not out.is_contiguous():
+        raise RuntimeError(f"linear: out must be a contiguous {shape} tensor")
+    rc = N.load().spd_linear(x.data_ptr(), weight.data_ptr(), _ptr(bias), out.data_ptr(), M, Nf, K, gc, M * gc,
+                             N.SPD_ACT_GELU if gelu else N.SPD_ACT_NONE, dtype_code(x.dtype), _ptr(error_word),
+                             _stream_handle())
+    N.check(rc, "spd_linear")
     return out
 
 

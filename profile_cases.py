@@ -18,7 +18,8 @@ Cases:
                 with the full 1500-position cross contexts (what serving attends) and
                 100-token self contexts, replayed
                 from its CUDA graph; launches run inside an NVTX range named "steps"
-  decode_large  the same for random-init Whisper-large-v3 (bf16) with the full
+  decode_large  the same for random-init Whisper-large-v3 (bf16)
+  linear_table  the decode step's Linear shapes at batch 64, tcgen05 kernel vs cuBLAS with the full
                 1500-position cross contexts the serving configuration attends
 
 Each launch reads a different input set (``--sets``) so that DRAM counters see cold data.
@@ -147,6 +148,72 @@ def _decode_small(torch, ops, dev, sets, B=64, cross_len=1500, self_len=100, arc
     return run
 
 
+def _linear_table(torch, ops, dev):
+    """The decode step's Linear shapes at batch 64: the tcgen05 kernel against cuBLAS
+    (torch F.linear), each timed over 30 launches in a CUDA graph, rotating over enough
+    weight copies that every launch reads its weights from HBM (> 256 MB per rotation)."""
+    import torch.nn.functional as F
+
+    shapes = [("small q|k|v", 2304, 768, 3, False), ("small d x d", 768, 768, 1, False),
+              ("small fc1+gelu", 3072, 768, 1, True), ("small fc2", 768, 3072, 1, False),
+              ("small head", 51865, 768, 1, False), ("large q|k|v", 3840, 1280, 3, False),
+              ("large d x d", 1280, 1280, 1, False), ("large fc1+gelu", 5120, 1280, 1, True),
+              ("large fc2", 1280, 5120, 1, False), ("large head", 51866, 1280, 1, False)]
+    M = 64
+    for name, Nf, K, groups, gelu in shapes:
+        copies = max(2, -(-(256 << 20) // (Nf * K * 2)))
+        ws = [(torch.randn(Nf, K, device=dev) * K ** -0.5).half() for _ in range(copies)]
+        b = torch.zeros(Nf, device=dev).half()
+        x = torch.randn(M, K, device=dev).half()
+        outs = {}
+        for impl in ("tcgen05", "cublas"):
+            def run(i, impl=impl):
+                w = ws[i % copies]
+                if impl == "tcgen05":
+                    return ops.linear(x, w, b, gelu=gelu, groups=groups)
+                y = F.linear(x, w, b)
+                return F.gelu(y) if gelu else y
+            stream = torch.cuda.Stream(device=dev)
+            stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(stream):
+                for i in range(3):
+                    run(i)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(30):
+                    run(i)
+            with torch.cuda.stream(stream):
+                g.replay()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            outs[impl] = e0.elapsed_time(e1) * 1000.0 / 30
+            del g
+        wb = Nf * K * 2
+        print(f"{name:16s} N={Nf:6d} K={K:5d}: tcgen05 {outs['tcgen05']:7.2f} us ({wb / outs['tcgen05'] / 1e3:6.0f} GB/s)"
+              f"  cuBLAS {outs['cublas']:7.2f} us ({wb / outs['cublas'] / 1e3:6.0f} GB/s)")
+        del ws
+
+
+def _linear_dxd(torch, ops, dev, sets):
+    """One Whisper-small d x d projection at batch 64 (N = K = 768), rotating over enough
+    weight copies (> 256 MB) that each launch reads its weights from HBM."""
+    copies = 224
+    ws = [(torch.randn(768, 768, device=dev) * 0.036).half() for _ in range(copies)]
+    b = torch.zeros(768, device=dev).half()
+    x = torch.randn(64, 768, device=dev).half()
+    out = torch.empty(64, 768, device=dev).half()
+    WORK["linear_dxd"] = (768 * 768 * 2, "GB/s", None)
+    return lambda i: ops.linear(x, ws[i % copies], b, out=out)
+
+
+LIN_POINTS = ["entry", "set-up done", "griddepcontrol.wait returned", "first stage landed", "accumulator ready",
+              "partials exchanged", "outputs stored", "exit"]
+
+
 CASES = {
     "paged_cfg2": lambda t, o, dev, n: _paged(t, o, dev, n),
     "paged_big": lambda t, o, dev, n: _paged(t, o, dev, n, B=512, NB=16384, lo=448, name="paged_big"),
@@ -155,6 +222,7 @@ CASES = {
     "proj_small": lambda t, o, dev, n: _proj(t, o, dev, n, 768, 12, 12, "proj_small"),
     "proj_large": lambda t, o, dev, n: _proj(t, o, dev, n, 1280, 32, 20, "proj_large"),
     "decode_small": lambda t, o, dev, n: _decode_small(t, o, dev, n),
+    "linear_dxd": lambda t, o, dev, n: _linear_dxd(t, o, dev, n),
     "decode_large": lambda t, o, dev, n: _decode_small(t, o, dev, n, cross_len=1500, arch="whisper-large-v3",
                                                        dtype_name="bfloat16", name="decode_large"),
 }
@@ -164,18 +232,18 @@ POINTS = {0: ["entry", "first lengths scanned", "first copy issued", "producer o
           1: ["entry", "griddepcontrol.wait returned", "done"]}
 
 
-def _fetch_trace(lib):
+def _fetch_trace(lib, fn_name="spd_trace_fetch_paged"):
     import ctypes as C
 
     import numpy as np
 
     kernels, ctas, points = 2, 1024, 12
     buf = (C.c_ulonglong * (kernels * ctas * points))()
-    fn = lib.spd_trace_fetch_paged
+    fn = getattr(lib, fn_name)
     fn.restype = C.c_int
     fn.argtypes = [C.c_void_p, C.c_size_t]
     if fn(C.addressof(buf), kernels * ctas * points) != 0:
-        raise RuntimeError("spd_trace_fetch_paged failed")
+        raise RuntimeError(f"{fn_name} failed")
     return np.frombuffer(buf, dtype=np.uint64).reshape(kernels, ctas, points).astype(np.float64)
 
 
@@ -208,7 +276,7 @@ def _summarise_trace(tr):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=sorted(CASES))
+    ap.add_argument("case", choices=sorted(CASES) + ["linear_table"])
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--sets", type=int, default=2)
     ap.add_argument("--time", type=int, default=0, help="time this many plain launches with CUDA events")
@@ -225,6 +293,9 @@ def main():
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if a.case == "linear_table":
+        _linear_table(torch, ops, dev)
+        return
     run = CASES[a.case](torch, ops, dev, a.sets)
     nvtx = getattr(run, "captures_graph", False)
     if nvtx:
@@ -273,7 +344,18 @@ def main():
         us = s.elapsed_time(e) * 1000.0 / k
         w = sum(per[i % a.sets] for i in range(k)) / k if per else work
         print(f"{a.case}: {us:.2f} us per launch ({k} launches in a CUDA graph), {w / (us * 1e-6) / scale:.1f} {unit}")
-        if a.trace:
+        if a.trace and a.case.startswith("linear"):
+            tr = _fetch_trace(_native.load(), "spd_trace_fetch_linear")[0]
+            live = tr[:, 0] > 0
+            t0 = tr[live, 0].min()
+            for pt, name in enumerate(LIN_POINTS):
+                v = tr[live, pt]
+                v = v[v > 0]
+                if v.size:
+                    us = (v - t0) / 1e3
+                    print(f"{pt} {name:<32s} {v.size:5d} {us.min():7.2f} {float(sorted(us)[len(us) // 2]):8.2f} "
+                          f"{us.max():8.2f}")
+        elif a.trace:
             _summarise_trace(_fetch_trace(_native.load()))
 
 
