@@ -291,7 +291,7 @@ SERVING = {
     "config4": dict(arch="whisper-small", dtype="float16", n=256, rate=None, out=(20, 200), mels=80,
                     desc="random-init Whisper-small, fp16, 256-request burst, audio U[2,30] s, outputs U{20..200}"),
     "config5": dict(arch="whisper-large-v3", dtype="bfloat16", n=2048, rate=64.0, out=(20, 224), mels=128,
-                    desc="random-init Whisper-large-v3, bf16, Poisson 64 req/s per GPU, audio U[2,30] s, "
+                    hf_self_check=True, desc="random-init Whisper-large-v3, bf16, Poisson 64 req/s per GPU, audio U[2,30] s, "
                          "outputs U{20..224}"),
     "config5_burst": dict(arch="whisper-large-v3", dtype="bfloat16", n=512, rate=None, out=(20, 224), mels=128,
                           desc="capacity of the config-5 engine: random-init Whisper-large-v3, bf16, all requests "
@@ -382,18 +382,34 @@ def serving_leg(name, n_req, dev, rank, world, models):
     if name == "config1":
         out["tokens"] = r["tokens_by_request"]
     elif rank == 0:
-        from speech_serving.hf_reference import hf_greedy_tokens, sequence_agreement
+        from speech_serving.hf_reference import (NEAR_TIE_STEPS, hf_greedy_tokens, hf_top2_margins,
+                                                 near_tie_divergences, sequence_agreement)
 
+        t_check = time.perf_counter()
         k = min(AGREEMENT_SAMPLE, len(reqs))
         mels = torch.stack([q.mel for q in reqs[:k]])
-        ref = hf_greedy_tokens(model, mels, WHISPER_DEFAULT_PREFIX_TOKENS, [q.max_new_tokens for q in reqs[:k]],
-                               batch=32)
-        a = sequence_agreement(r["tokens_by_request"][:k], ref)
-        out["hf_sequence_agreement"] = {"requests": a["requests"], "identical": a["identical"],
-                                        "identical_frac": round(a["identical_frac"], 4),
-                                        "first_divergence": a["first_divergence"],
-                                        "sample": f"the first {k} requests of rank 0, re-decoded greedily by the "
-                                                  "unpatched HF decoder on the same weights, device and dtype"}
+        lens = [q.max_new_tokens for q in reqs[:k]]
+        ours = r["tokens_by_request"][:k]
+        ref = hf_greedy_tokens(model, mels, WHISPER_DEFAULT_PREFIX_TOKENS, lens, batch=32)
+        a = sequence_agreement(ours, ref)
+        ties = near_tie_divergences(ours, ref, hf_top2_margins(model, mels, WHISPER_DEFAULT_PREFIX_TOKENS, ref), dtype)
+        agree = {"requests": a["requests"], "identical": a["identical"],
+                 "identical_frac": round(a["identical_frac"], 4), "first_divergence": a["first_divergence"],
+                 "divergences_at_near_tie": ties["at_near_tie"],
+                 "requests_without_near_tie": ties["requests_without_near_tie"],
+                 "identical_without_near_tie": ties["identical_without_near_tie"],
+                 "near_tie": f"HF top-1 minus top-2 logit within {NEAR_TIE_STEPS} steps of the {cfg['dtype']} grid "
+                             "at the divergent position (HF teacher-forced on its own sequence)",
+                 "sample": f"the first {k} requests of rank 0, re-decoded greedily by the unpatched HF decoder "
+                           "(batch 32) on the same weights, device and dtype"}
+        if cfg.get("hf_self_check"):
+            # the HF decoder against itself at another batch size: the agreement floor that
+            # ties in this dtype leave to any second implementation
+            self_a = sequence_agreement(hf_greedy_tokens(model, mels, WHISPER_DEFAULT_PREFIX_TOKENS, lens, batch=8), ref)
+            agree["hf_self_agreement"] = {"identical": self_a["identical"], "requests": self_a["requests"],
+                                          "what": "HF decoder at batch 8 against HF at batch 32, same requests"}
+        agree["check_s"] = round(time.perf_counter() - t_check, 1)
+        out["hf_sequence_agreement"] = agree
     del sched
     torch.cuda.empty_cache()
     return out

@@ -307,3 +307,39 @@ def test_hf_greedy_reference_matches_plain_hf_decoding():
     assert got == want
     a = sequence_agreement(got, [want[0], want[1][:3] + [want[1][3] + 1], want[2]])
     assert a["identical"] == 2 and a["first_divergence"] == [3]
+
+
+def test_hf_margins_and_near_tie_classification():
+    """hf_top2_margins teacher-forces ragged sequences (right-padded in a batch) and gives
+    each position's HF top-1 minus top-2 logit; on HF's own greedy sequences every top-1 is
+    the sequence's token, so every margin is >= 0 and equals the one from an unbatched
+    pass.  near_tie_divergences marks a divergence as a near-tie only within the given
+    number of grid steps of the top-1 logit."""
+    from transformers import WhisperConfig
+
+    from speech_serving.hf_reference import grid_step, hf_greedy_tokens, hf_top2_margins, near_tie_divergences
+    from speech_serving.models import PretrainedWhisperModel
+
+    cfg = WhisperConfig(vocab_size=320, num_mel_bins=16, encoder_layers=2, decoder_layers=2, d_model=64,
+                        encoder_attention_heads=4, decoder_attention_heads=4, encoder_ffn_dim=128, decoder_ffn_dim=128,
+                        max_source_positions=20, max_target_positions=64, pad_token_id=300, bos_token_id=301,
+                        eos_token_id=301, decoder_start_token_id=302, init_std=0.2)
+    model = PretrainedWhisperModel(config=cfg, device="cpu", dtype=torch.float32, seed=0)
+    torch.manual_seed(2)
+    mels = torch.randn(3, 16, 40)
+    prompt = [302, 303]
+    ref = hf_greedy_tokens(model, mels, prompt, [6, 3, 5], batch=3)
+    m3 = hf_top2_margins(model, mels, prompt, ref, batch=3)
+    m1 = hf_top2_margins(model, mels, prompt, ref, batch=1)
+    assert [len(r) for r in m3] == [6, 3, 5]
+    for ra, rb in zip(m3, m1):
+        for (ma, ta), (mb, tb) in zip(ra, rb):
+            assert ma >= 0 and abs(ma - mb) < 1e-4 and abs(ta - tb) < 1e-4
+    assert grid_step(3.0, torch.bfloat16) == 2.0 ** -6 and grid_step(3.0, torch.float16) == 2.0 ** -9
+    ours = [list(ref[0]), ref[1][:1] + [ref[1][1] + 1] + ref[1][2:], list(ref[2])]
+    margin, top = m3[1][1]
+    wide = near_tie_divergences(ours, ref, m3, torch.float32, steps=int(margin / grid_step(top, torch.float32)) + 2)
+    assert wide["at_near_tie"] == 1 and wide["divergences"][0]["position"] == 1
+    tight = near_tie_divergences(ours, ref, m3, torch.float32, steps=0)
+    assert tight["at_near_tie"] == 0 and tight["requests_without_near_tie"] == 3
+    assert tight["identical_without_near_tie"] == 2

@@ -17,15 +17,14 @@ and sequences must be identical on >= 99 % of requests.  In bf16 the large-v3 lo
 often tie to within one bf16 step (see the test's docstring), which no two
 implementations with different summation orders resolve alike; there the test checks that
 divergences happen only at such ties."""
-import math
-
 import pytest
 import torch
 
 from speech_serving.block_manager import BlockManager
 from speech_serving.dual_cache_manager import DualCacheManager
 from speech_serving.encoder_block_manager import EncoderBlockManager
-from speech_serving.hf_reference import hf_greedy_tokens, sequence_agreement
+from speech_serving.hf_reference import (hf_greedy_tokens, hf_top2_margins, near_tie_divergences,
+                                         sequence_agreement)
 from speech_serving.memory_guard import MemoryGuard
 from speech_serving.models import PretrainedWhisperModel
 from speech_serving.phase_aware_scheduler import WHISPER_DEFAULT_PREFIX_TOKENS, PhaseAwareSpeechScheduler
@@ -45,32 +44,6 @@ def _engine(model, dtype):
                                      graph_direct_encoder_kv=True), dec
 
 
-def _hf_margins(model, mels, prompt, seqs, batch=16):
-    """For every request, the HF decoder's top-1 minus top-2 logit and the top-1 logit at
-    each position of ``seqs`` (teacher-forced on the prompt and the sequence so far), in
-    the model's dtype, with the suppress mask applied."""
-    hf = model.hf_model
-    out = []
-    with torch.no_grad():
-        for lo in range(0, len(seqs), batch):
-            hi = min(len(seqs), lo + batch)
-            e = hf.model.encoder(mels[lo:hi].to(DEV, model.dtype)).last_hidden_state
-            ids = torch.tensor([list(prompt) + list(s[:-1]) for s in seqs[lo:hi]], device=DEV)
-            h = hf.model.decoder(input_ids=ids, encoder_hidden_states=e).last_hidden_state[:, len(prompt) - 1:]
-            lg = hf.proj_out(h)
-            if model.suppress_mask is not None:
-                lg = lg.masked_fill(model.suppress_mask, float("-inf"))
-            top = lg.float().topk(2, dim=-1).values  # [b, positions, 2]
-            for marg, best in zip((top[..., 0] - top[..., 1]).tolist(), top[..., 0].tolist()):
-                out.append(list(zip(marg, best)))
-    return out
-
-
-def _ulp(x: float, dtype) -> float:
-    """Spacing of ``dtype`` numbers at magnitude |x|."""
-    return float(torch.finfo(dtype).eps) * 2.0 ** math.floor(math.log2(max(abs(x), 1e-30)))
-
-
 @pytest.mark.parametrize("arch,dtype,n_mels", [("whisper-small", torch.float16, 80),
                                                ("whisper-large-v3", torch.float16, 128),
                                                ("whisper-large-v3", torch.bfloat16, 128)])
@@ -80,8 +53,8 @@ def test_serving_sequences_match_hf_decoder(arch, dtype, n_mels):
     two logits within a few steps of the 16-bit grid of each other (logits near 3 are
     2^-9 apart in fp16, 2^-6 in bf16), so the HF decoder itself changes tokens with the
     batch size.  There every divergence must fall on such a near-tie (HF top-2 margin
-    within NEAR_TIE_STEPS steps of the dtype's grid), the requests whose HF path has no
-    near-tie must be >= 99 % identical, and our agreement with HF must be at least HF's own
+    within hf_reference.NEAR_TIE_STEPS steps of the dtype's grid), the requests whose HF
+    path has no near-tie must be >= 99 % identical, and our agreement with HF must be at least HF's own
     batch-size self-agreement (up to 6 of 64 requests of sampling noise)."""
     model = PretrainedWhisperModel(config=whisper_config(arch), device=DEV, dtype=dtype, seed=0)
     reqs = synthetic_requests(N_REQ, n_mels, seed=2024, out_lo=N_TOK, out_hi=N_TOK)
@@ -102,27 +75,17 @@ def test_serving_sequences_match_hf_decoder(arch, dtype, n_mels):
         return
     ref8 = hf_greedy_tokens(model, mels, prompt, N_TOK, batch=8)
     self_agree = sequence_agreement(ref8, ref)
-    per_req = _hf_margins(model, mels, prompt, ref, batch=16)
-    per_req4 = _hf_margins(model, mels, prompt, ref, batch=4)
+    per_req = hf_top2_margins(model, mels, prompt, ref, batch=16)
+    per_req4 = hf_top2_margins(model, mels, prompt, ref, batch=4)
     noise = max(abs(a[0] - b[0]) for ra, rb in zip(per_req, per_req4) for a, b in zip(ra, rb))
-    near = [[m <= NEAR_TIE_STEPS * _ulp(top, dtype) for m, top in row] for row in per_req]
-    div = []
-    for i, (a, b) in enumerate(zip(ours, ref)):
-        if a != b:
-            k = next(j for j, (x, y) in enumerate(zip(a, b)) if x != y)
-            m, top = per_req[i][k]
-            div.append({"request": i, "position": k, "ours": a[k], "hf": b[k], "hf_margin": round(m, 5),
-                        "steps": round(m / _ulp(top, dtype), 2), "near_tie": near[i][k]})
-    clean = [i for i in range(N_REQ) if not any(near[i])]
-    clean_same = sum(ours[i] == ref[i] for i in clean)
+    ties = near_tie_divergences(ours, ref, per_req, dtype)
+    div, clean, clean_same = ties["divergences"], ties["requests_without_near_tie"], ties["identical_without_near_tie"]
     print(f"HF batch 8 vs HF batch 32: {self_agree['identical']}/{self_agree['requests']} identical; HF "
           f"teacher-forced top-2 margin differs by up to {noise:.5f} between batch 16 and batch 4; requests "
-          f"with no near-tie on their HF path: {len(clean)}, identical: {clean_same}; divergences: {div}")
+          f"with no near-tie on their HF path: {clean}, identical: {clean_same}; divergences: {div}")
     assert all(d["near_tie"] for d in div), div
-    assert clean_same >= 0.99 * len(clean)
+    assert clean_same >= 0.99 * clean
     # as close to the HF decoder as the HF decoder is to itself at another batch size
     # (up to sampling noise on 64 requests)
     assert agree["identical"] >= self_agree["identical"] - 6, (agree["identical"], self_agree["identical"])
 
-
-NEAR_TIE_STEPS = 8
