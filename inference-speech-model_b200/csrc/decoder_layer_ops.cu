@@ -14,9 +14,8 @@
 // Both kernels here are launched with programmatic dependent launch: they signal
 // launch_dependents on entry, so a PDL-launched kernel behind them (the small-batch GEMM
 // that consumes the LayerNorm output) gets resident and prefetches its weights while
-// they run, and they wait (griddepcontrol.wait) for the kernel before them only when
-// they first read an input it may have written; gamma and beta are parameters, read
-// before that wait.
+// they run.  Every input, parameters included, is read after griddepcontrol.wait, so
+// results never depend on what the kernel before them writes.
 #include "spd_params.cuh"
 
 namespace spd {
@@ -51,6 +50,7 @@ __global__ void __launch_bounds__(128) add_layernorm_kernel(const AddLnParams p)
   const int nvec = p.cols / E;
   const T* x = reinterpret_cast<const T*>(p.x) + row * p.cols;
   const T* dl = p.delta ? reinterpret_cast<const T*>(p.delta) + row * p.cols : nullptr;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // x, delta, gamma, beta: written before this kernel
   // gamma and beta do not depend on the row: with few vectors per lane they are loaded up
   // front, so their latency overlaps the row's loads and reductions instead of following them
   constexpr bool kPrefetch = VPL <= 4;
@@ -65,7 +65,6 @@ __global__ void __launch_bounds__(128) add_layernorm_kernel(const AddLnParams p)
       }
     }
   }
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // x and delta may come from the previous kernel
   float v[VPL][E];
   float sum = 0.f;
 #pragma unroll

@@ -14,13 +14,16 @@
 //   warp 1 lane 0 issues tcgen05.mma (kind::f16, fp32 accumulation in 64 TMEM columns).
 // * Small N leaves most SMs idle, so K is split over a thread-block cluster of ks CTAs
 //   (ks in 1..8, chosen so the grid fills the SMs): each CTA writes its fp32 partial tile
-//   to its own shared memory, and after a cluster barrier rank r sums features
-//   [r*128/ks, (r+1)*128/ks) over all ranks through distributed shared memory, adds the
-//   bias, applies the activation, rounds once and stores.  A second cluster barrier keeps
-//   every rank's shared memory alive until the others have read it.
+//   to its own shared memory; after a cluster barrier (every rank's receive barrier armed)
+//   each rank pushes to rank r the slice of features [r*128/ks, (r+1)*128/ks) with a bulk
+//   shared::cluster copy that completes on rank r's mbarrier.  Rank r then sums its
+//   features over all ranks from its own shared memory, adds the bias, applies the
+//   activation, rounds once and stores.  A second cluster barrier keeps every rank alive
+//   until the copies it sent have landed.
 // * Launched with programmatic dependent launch: before griddepcontrol.wait the CTA only
-//   sets up barriers and TMEM and prefetches its W slices into L2 (W is a parameter, not
-//   an output of the previous kernel); X is loaded after the wait.
+//   sets up barriers and TMEM and prefetches its W slices into L2 (a hint: the tiles and
+//   the bias are read after the wait, so results never depend on what the previous kernel
+//   writes).
 // * Output columns may be grouped: column n goes to plane n / group_cols (planes
 //   group_stride elements apart) as [M][group_cols] — how a packed q|k|v weight writes
 //   three separate [M][H*D] tensors.
@@ -141,14 +144,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // the bias of the feature this thread stores (a parameter: read before the wait)
-  constexpr int F = BF / KS;
-  const int n = n0 + kr * F + tid % F;
-  const float bn = (p.bias && n < p.N) ? Elem<T>::to_f(__ldg(reinterpret_cast<const T*>(p.bias) + n)) : 0.f;
   if (tid == 0) LIN_TRACE(1);
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0) LIN_TRACE(2);
+  // the bias of the feature this thread stores: loaded now, used only in the epilogue
+  constexpr int F = BF / KS;
+  const int n = n0 + kr * F + tid % F;
+  const float bn = (p.bias && n < p.N) ? Elem<T>::to_f(__ldg(reinterpret_cast<const T*>(p.bias) + n)) : 0.f;
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ------------------------------------------------------------------

@@ -64,3 +64,40 @@ def test_single_process_fallbacks():
         replicas.shard([1], 2, 2)
     with pytest.raises(ValueError):
         replicas.whole_job_rate(1, 0)
+
+
+def _dying_worker(rank, world, port, q):
+    """Rank 1 dies after joining the group (a replica whose serving loop crashed); rank 0
+    then aggregates as bench.py does and must get an error, not hang."""
+    import time
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    if rank == 1:
+        os._exit(3)
+    t0 = time.monotonic()
+    try:
+        replicas.max_over_ranks(1.0)
+        q.put(("returned", time.monotonic() - t0))
+    except Exception as e:  # the collective's error on a lost peer or its timeout
+        q.put(("raised", type(e).__name__, time.monotonic() - t0))
+    os._exit(0)  # the group is broken: leave without a collective teardown
+
+
+def test_lost_rank_ends_the_aggregation_with_an_error():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == "raised", res
+    assert res[-1] < 60.0  # bounded by the group's timeout, not a hang
+    assert procs[1].exitcode == 3 and procs[0].exitcode == 0
