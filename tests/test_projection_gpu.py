@@ -69,13 +69,15 @@ def test_projection_whisper_small_shape_vs_torch(dtype):
     assert bool((out[0] == 7.0).all()) and bool((out[2] == 7.0).all())
 
 
-def test_projection_partial_tiles_and_graph_capture():
-    """N = 1*2*5*64 = 640 (not a multiple of the 256-wide tile), T = 300 < T_out."""
+@pytest.mark.parametrize("d", [128, 1024])
+def test_projection_partial_tiles_and_graph_capture(d):
+    """N = 1*2*5*64 = 640 (not a multiple of the 256-wide tile), T = 300 < T_out; d_model
+    128 runs the one-CTA form, 1024 the CTA-pair form."""
     torch.manual_seed(1)
-    B, T, d, L, H, D, T_out = 3, 300, 128, 1, 5, 64, 320
+    B, T, L, H, D, T_out = 3, 300, 1, 5, 64, 320
     dtype = torch.float16
     enc = torch.randn(B, T, d, device="cuda").to(dtype)
-    w = (torch.randn(L * 2 * H * D, d, device="cuda") * 0.05).to(dtype)
+    w = (torch.randn(L * 2 * H * D, d, device="cuda") * d ** -0.5).to(dtype)
     out = torch.zeros((B, L, 2, H, T_out, D), dtype=dtype, device="cuda")
     g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
@@ -92,3 +94,19 @@ def test_projection_partial_tiles_and_graph_capture():
     ok, err = _close(out[:, :, :, :, :T], ref, dtype)
     assert ok, err
     assert not out[:, :, :, :, T:].any()
+
+
+@pytest.mark.parametrize("B,T,d,L,H", [(1, 100, 256, 1, 4), (1, 200, 1280, 2, 20), (3, 1500, 1280, 1, 20)])
+def test_projection_row_tails_and_large_v3_width(B, T, d, L, H):
+    """Row counts that leave the second half of a 256-row tile partly or wholly past M
+    (M = 100, 200, 4500), and large-v3's d_model (K = 1280: 20 K slices per tile)."""
+    torch.manual_seed(B * 7 + T)
+    D, dtype = 64, torch.bfloat16
+    enc = torch.randn(B, T, d, device="cuda").to(dtype)
+    w = (torch.randn(L * 2 * H * D, d, device="cuda") * d ** -0.5).to(dtype)
+    bias = (torch.randn(L * 2 * H * D, device="cuda") * 0.1).to(dtype)
+    out = torch.full((B, L, 2, H, T, D), float("nan"), dtype=dtype, device="cuda")
+    ops.cross_kv_project(enc, w, bias, out)
+    ref = (enc.float().reshape(B * T, d) @ w.float().t() + bias.float()).view(B, T, L, 2, H, D)
+    ok, err = _close(out, ref.permute(0, 2, 3, 4, 1, 5), dtype)
+    assert ok, err
