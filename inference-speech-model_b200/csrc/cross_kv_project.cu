@@ -15,8 +15,8 @@
 // tiles for each 64-wide K slice into a 4-stage shared-memory ring (full/empty
 // mbarriers); warp 1 lane 0 issues tcgen05.mma (kind::f16, M=128, N=256, K=16) into one
 // of two 256-column fp32 TMEM accumulators, frees each stage with tcgen05.commit and
-// signals a finished tile with a commit on that accumulator's barrier; warps 2..5 are
-// the epilogue, one accumulator row (TMEM lane) per thread: tcgen05.ld, the bias in
+// signals a finished tile with a commit on that accumulator's barrier; warps 2..9 are
+// the epilogue, one accumulator row (TMEM lane) and half the columns per thread: tcgen05.ld, the bias in
 // fp32, rounding, and 16-byte stores of one head's row into the slot layout, after which
 // the accumulator is handed back.  So tile i's epilogue overlaps tile i+1's MMAs.  All
 // waits are bounded (SPD_DEVERR_TIMEOUT on expiry).
@@ -81,16 +81,28 @@ __device__ __forceinline__ void store_row_chunk(const float* v, int n_first, int
 // Persistent, warp-specialised: CTA c computes tiles c, c + G, c + 2G, ... (G CTAs).
 //   warp 0        TMA producer: A and W K-slices into the STAGES-deep shared ring
 //   warp 1        MMA issuer: each tile into one of two TMEM accumulators (2 x 256 columns)
-//   warps 2..5    epilogue: TMEM -> registers -> bias -> slot layout; warp w reads TMEM
-//                 lanes 32*(w%4).., so the four warps cover the 128 accumulator rows
+//   warps 2..     epilogue: TMEM -> registers -> bias -> slot layout; warp w reads TMEM
+//                 lanes 32*(w%4).., so each group of four warps covers the 128
+//                 accumulator rows, and the groups split the columns
 // The epilogue of tile i runs while the MMAs of tile i+1 fill the other accumulator.
-constexpr int kProjThreads = 192;
+#ifndef SPD_PROJ_EPI_WARPS
+#define SPD_PROJ_EPI_WARPS 8
+#endif
+// Epilogue warps: 4 or 8 (or 16).  Warp w may only read TMEM lanes 32*(w%4).., so with 8
+// the two warps of a lane quarter split the accumulator's columns.  Eight drain a tile
+// fast enough that the MMAs no longer wait for the accumulator (Whisper-small handoff
+// 68 -> 52.5 us, large-v3 341 -> 277.5 us per request, against four).
+constexpr int kEpiWarps = SPD_PROJ_EPI_WARPS;
+constexpr int kProjThreads = 64 + 32 * kEpiWarps;
 constexpr int kAccBufs = 2;
 #ifndef SPD_PROJ_PAIRS
 #define SPD_PROJ_PAIRS 1
 #endif
 constexpr bool kProjPairs = SPD_PROJ_PAIRS != 0;  // use the CTA-pair form when it launches
-constexpr int kPairMinK = 1024;                    // ... and d_model is at least this
+#ifndef SPD_PROJ_PAIR_MIN_K
+#define SPD_PROJ_PAIR_MIN_K 1024
+#endif
+constexpr int kPairMinK = SPD_PROJ_PAIR_MIN_K;     // ... and d_model is at least this
 
 template <typename T>
 __global__ void __launch_bounds__(kProjThreads, 1)
@@ -121,7 +133,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
     }
     for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[b], kEpiWarps);  // one arrival per epilogue warp
     }
     fence_barrier_init();
   }
@@ -187,6 +199,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
   } else {
     // ---- epilogue: thread = accumulator row (TMEM lane 32*(warp%4) + lane) ---------------
     const int q = warp & 3;
+    constexpr int kCols = BN * 4 / kEpiWarps;  // accumulator columns per epilogue warp
+    const int c_begin = ((warp - 2) / 4) * kCols;
     const T* bias = reinterpret_cast<const T*>(p.bias);
     const int HD = p.H * p.D;
     const long long plane = (long long)p.T_out * p.D;  // one (layer, k|v, head) plane
@@ -204,7 +218,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
       const long long slot = row_ok ? (p.slot_ids ? p.slot_ids[b] : b) : 0;
       T* out = reinterpret_cast<T*>(p.out) + slot * p.out_slot_stride + (long long)t * p.D;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = c_begin; c0 < c_begin + kCols; c0 += 16) {
         float v[16];
         tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TMEM_COLS + c0), v);  // all lanes
         if (!row_ok) continue;
@@ -247,8 +261,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
 //                 full barrier (rank 0 arms it for both)
 //   warp 1        rank 0: MMA issuer; each stage is released to both producers and each
 //                 finished tile to both epilogues by one tcgen05.commit per CTA
-//   warps 2..5    epilogue of this CTA's 128 rows; the four warps of each CTA arrive on
-//                 rank 0's accumulator-empty barrier (8 arrivals)
+//   warps 2..     epilogue of this CTA's 128 rows; every epilogue warp of each CTA
+//                 arrives on rank 0's accumulator-empty barrier
 // Every wait is bounded.  On an error both CTAs still pass both cluster barriers, and
 // rank 0 waits (bounded) for the stages either producer issued before the CTAs exit, so
 // no copy lands in the shared memory of a CTA that has left.
@@ -305,7 +319,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kProjThreads, 1)
     }
     for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 8);  // rank 0's: the four epilogue warps of each CTA
+      mbar_init(&acc_empty[b], 2 * kEpiWarps);  // rank 0's: the epilogue warps of both CTAs
     }
     *issued_slot = 0;
     fence_barrier_init();
@@ -373,6 +387,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kProjThreads, 1)
   } else {
     // ---- epilogue (both ranks): thread = accumulator row of this CTA --------------------
     const int q = warp & 3;
+    constexpr int kCols = P_TILE_N * 4 / kEpiWarps;  // accumulator columns per epilogue warp
+    const int c_begin = ((warp - 2) / 4) * kCols;
     const T* bias = reinterpret_cast<const T*>(p.bias);
     const int HD = p.H * p.D;
     const long long plane = (long long)p.T_out * p.D;
@@ -391,7 +407,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kProjThreads, 1)
       const long long slot = row_ok ? (p.slot_ids ? p.slot_ids[b] : b) : 0;
       T* out = reinterpret_cast<T*>(p.out) + slot * p.out_slot_stride + (long long)t * p.D;
 #pragma unroll 1
-      for (int c0 = 0; c0 < P_TILE_N; c0 += 32) {
+      for (int c0 = c_begin; c0 < c_begin + kCols; c0 += 32) {
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TMEM_COLS + c0), v);  // all lanes
         if (!row_ok) continue;
