@@ -117,20 +117,36 @@ def _padded_head(model: nn.Module, linear: nn.Linear, multiple: int = 64) -> tor
 
 def _tc_linear_ok(x: torch.Tensor, K: int) -> bool:
     """True when ``ops.linear`` (the small-batch tcgen05 GEMM) takes this input: 16-bit,
-    at most 64 rows, K a multiple of 64.  The decode steps use it for the MLP: fc1 with
-    its GELU fused (one launch instead of a GEMM and an elementwise kernel) and fc2, which
-    measured at least even with cuBLAS at batch 64.  The q/k/v and d x d projections and
+    at most 64 rows, K a multiple of 64.  The decode steps use it for the MLP of models
+    up to TC_MLP_MAX_WEIGHT_BYTES per layer: fc1 with its GELU fused (one launch instead
+    of a GEMM and an elementwise kernel) and fc2.  The q/k/v and d x d projections and
     the vocabulary-padded head stay on cuBLAS, which measured faster for those shapes
     (profile_cases.py linear_table, and the decode_small / decode_large steps)."""
     return x.dtype in (torch.float16, torch.bfloat16) and x.shape[0] <= 64 and K % 64 == 0
 
 
+# An MLP Linear runs on the tcgen05 kernel up to this weight size, else on cuBLAS (plus a
+# GELU kernel after fc1).  Whole decode steps at batch 64 decided it: Whisper-small
+# (4.7 MB per layer) 1,253 us with both MLP layers on the kernel against 1,256 us on
+# cuBLAS; large-v3 (13.1 MB) 4,725 us against 4,691 us.
+TC_MLP_MAX_WEIGHT_BYTES = 8 << 20
+
+
+def _tc_mlp_ok(x: torch.Tensor, lin: nn.Linear) -> bool:
+    return (_tc_linear_ok(x, lin.in_features)
+            and lin.weight.numel() * lin.weight.element_size() <= TC_MLP_MAX_WEIGHT_BYTES)
+
+
 def _mlp(h: torch.Tensor, fc1: nn.Linear, fc2: nn.Linear, act_is_gelu: bool, act) -> torch.Tensor:
-    """fc2(act(fc1(h))), with fc1 + GELU and fc2 on the tcgen05 kernel when it applies."""
-    if act_is_gelu and _tc_linear_ok(h, fc1.in_features) and fc2.in_features % 64 == 0:
+    """fc2(act(fc1(h))), with fc1 + GELU and fc2 on the tcgen05 kernel where that measured
+    faster (TC_MLP_MAX_WEIGHT_BYTES)."""
+    if act_is_gelu and _tc_mlp_ok(h, fc1):
         u = ops.linear(h.contiguous(), fc1.weight, fc1.bias, gelu=True)
-        return ops.linear(u, fc2.weight, fc2.bias)
-    return fc2(act(fc1(h)))
+    else:
+        u = act(fc1(h))
+    if _tc_mlp_ok(u, fc2):
+        return ops.linear(u.contiguous(), fc2.weight, fc2.bias)
+    return fc2(u)
 
 
 def _head_logits(model: nn.Module, h: torch.Tensor, head: nn.Linear) -> torch.Tensor:
