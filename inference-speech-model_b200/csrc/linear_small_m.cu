@@ -13,13 +13,15 @@
 //   W and X with 2-D TMA loads (128-byte swizzle, no multicast) through a 4-stage ring;
 //   warp 1 lane 0 issues tcgen05.mma (kind::f16, fp32 accumulation in 64 TMEM columns).
 // * Small N leaves most SMs idle, so K is split over a thread-block cluster of ks CTAs
-//   (ks in 1..8, chosen so the grid fills the SMs): each CTA writes its fp32 partial tile
-//   to its own shared memory; after a cluster barrier (every rank's receive barrier armed)
-//   each rank pushes to rank r the slice of features [r*128/ks, (r+1)*128/ks) with a bulk
-//   shared::cluster copy that completes on rank r's mbarrier.  Rank r then sums its
-//   features over all ranks from its own shared memory, adds the bias, applies the
-//   activation, rounds once and stores.  A second cluster barrier keeps every rank alive
-//   until the copies it sent have landed.
+//   (ks in 1..8, chosen so the grid fills the SMs).  Every rank arms its receive barrier
+//   and the cluster synchronises once in the prologue, before griddepcontrol.wait (the
+//   partial tile and the receive buffer have their own shared memory, past the ring).
+//   Once its fp32 partial tile is in shared memory, each rank pushes to rank r the slice
+//   of features [r*128/ks, (r+1)*128/ks) with a bulk shared::cluster copy that completes
+//   on rank r's mbarrier.  Rank r then sums its features over all ranks from its own
+//   shared memory, adds the bias, applies the activation, rounds once and stores.  A
+//   cluster barrier at the end keeps every rank alive until the copies it sent have
+//   landed.
 // * Launched with programmatic dependent launch: before griddepcontrol.wait the CTA only
 //   sets up barriers and TMEM and prefetches its W slices into L2 (a hint: the tiles and
 //   the bias are read after the wait, so results never depend on what the previous kernel
@@ -52,8 +54,9 @@ constexpr int X_BYTES = BR * BK * 2;  // 8 KB
 constexpr int PSTRIDE = BR + 4;       // floats per feature row of the partial tile (16-byte aligned rows)
 constexpr int RING_BYTES = STAGES * (W_BYTES + X_BYTES);
 constexpr int PART_BYTES = BF * PSTRIDE * 4;
-static_assert(2 * PART_BYTES <= RING_BYTES, "the partial tile and the receive buffer reuse the ring");
-constexpr size_t SMEM_BYTES = 1024 /*alignment slack*/ + RING_BYTES + 256;
+// the partial tile and the receive buffer sit after the ring, so peers may push into a
+// rank's receive buffer while its MMAs still read the ring
+constexpr size_t SMEM_BYTES = 1024 /*alignment slack*/ + RING_BYTES + 2 * PART_BYTES + 256;
 constexpr int kThreads = 128;
 constexpr int kMaxClusterK = 8;
 
@@ -110,14 +113,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* smem = smem_raw + ((1024 - (base_addr & 1023)) & 1023);  // 1024-aligned for SW128
   unsigned char* w_tiles = smem;
   unsigned char* x_tiles = smem + STAGES * W_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + RING_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + RING_BYTES + 2 * PART_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* recv_bar = acc_full + 1;  // the peers' slices of this CTA's features have landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
-  // over the ring once the MMAs are done: this CTA's partial tile [BF][PSTRIDE], then the
-  // receive buffer, one [BF / ks][PSTRIDE] slice per cluster rank
-  float* part = reinterpret_cast<float*>(smem);
+  // after the ring: this CTA's partial tile [BF][PSTRIDE], then the receive buffer, one
+  // [BF / ks][PSTRIDE] slice per cluster rank
+  float* part = reinterpret_cast<float*>(smem + RING_BYTES);
   float* recv = part + BF * PSTRIDE;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -140,8 +143,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     for (int i = 0; i < kper; ++i) tma_prefetch_2d(&tm_w, (kb0 + i) * BK, n0);
   }
+  // every rank's receive barrier is armed before any peer can push into it: the cluster
+  // barrier for that runs here, while the previous kernel in the stream may still run
+  constexpr int F = BF / KS;
+  constexpr uint32_t kSliceBytes = F * PSTRIDE * 4;
+  if (KS > 1 && tid == 0) mbar_arrive_expect_tx(recv_bar, (uint32_t)(KS - 1) * kSliceBytes);
   tc_fence_before();
   __syncthreads();
+  if (KS > 1) cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (tid == 0) LIN_TRACE(1);
@@ -149,7 +158,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0) LIN_TRACE(2);
   // the bias of the feature this thread stores: loaded now, used only in the epilogue
-  constexpr int F = BF / KS;
   const int n = n0 + kr * F + tid % F;
   const float bn = (p.bias && n < p.N) ? Elem<T>::to_f(__ldg(reinterpret_cast<const T*>(p.bias) + n)) : 0.f;
 
@@ -207,20 +215,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_proxy_async_smem();  // the partial tile is read by bulk copies (async proxy) next
   // ---- exchange: rank r receives every peer's slice of features [r*F, (r+1)*F) ---------
   // Each rank pushes its slices with bulk shared-to-shared copies (the copy engine, not
-  // per-thread remote loads); the first cluster barrier makes every rank's receive
-  // barrier armed and its ring idle before any copy lands.  Every rank sends even when
-  // its own accumulator was not ready, so every receive barrier completes.
-  constexpr uint32_t kSliceBytes = F * PSTRIDE * 4;
+  // per-thread remote loads) into receive buffers armed in the prologue; the CTA barrier
+  // orders this CTA's partial-tile writes before its copies read them.  Every rank sends
+  // even when its own accumulator was not ready, so every receive barrier completes.
+  __syncthreads();
   if (ks > 1) {
-    if (tid == 0) mbar_arrive_expect_tx(recv_bar, (uint32_t)(ks - 1) * kSliceBytes);
-    cluster_sync();
     if (tid < ks && tid != kr) {
       const uint32_t peer = (uint32_t)tid;
       bulk_copy_s2peer(dsmem_addr(recv + kr * F * PSTRIDE, peer), part + tid * F * PSTRIDE, kSliceBytes,
                        dsmem_addr(recv_bar, peer));
     }
-  } else {
-    __syncthreads();
   }
   if (tid == 0) LIN_TRACE(5);
   const bool got = ks == 1 || mbar_wait_bounded(recv_bar, 0, p.err);
